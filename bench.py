@@ -1,0 +1,386 @@
+#!/usr/bin/env python3
+"""bench.py -- headline benchmark of the B200 matrix-multiply hot path.
+
+Workload: Qwen2.5-0.5B-architecture FP16-weight decode,
+FP32 accumulate, random-init weights in the reference's file layout, 32
+seeded prompt tokens, 256 new tokens, batch 1, KV cache up to 2048.  One
+step = one generation request: prime the prompt, then decode 256 tokens.
+
+  value   decode tokens/s over all ranks (the reference's own metric:
+          generated tokens / generation-loop time, qwen_engine.c:549-551),
+          CUDA events on the engine stream around the 256 decode steps,
+          inputs resident, max over ranks.
+  e2e     the same metric through the public C-ABI call with host buffers:
+          sb_engine_generate (prompt ids in from pinned host memory,
+          generated ids out), whole call timed per step.
+  roofline  the dominant kernel of the step, timed standalone after an L2
+          flush, algorithmic bytes / time vs the measured HBM copy peak.
+
+N > 1 (torchrun): one independent replica per GPU (decode does not shard);
+scaling "weak".  The weights (988 MB) exceed the 126 MB L2, so no flush is
+needed between timed steps.
+
+`--impl reference` times the reference's own CPU decode (cpu_forward of
+gpu-llm/engine/qwen_engine.c compiled unmodified into oracle/_ref) on the
+host cores, one forked replica per core, on the same metric.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "switch-l4t-gpu_b200")
+sys.path.insert(0, PKG)
+
+N_PROMPT, N_GEN, MAX_CTX = 32, 256, 2048
+WEIGHT_SEED = 20261201
+METRIC = "Qwen-0.5B-shape FP16 decode tok/s"
+UNIT = "tok/s"
+BASELINE_TOKS = 8.9  # Qwen2.5-0.5B FP16 decode on Tegra X1 (gpu-llm/STATUS.md:112)
+FALLBACK_HBM_GBS = 6650.0
+CONFIG = {
+    "workload": "qwen2.5-0.5b-fp16-decode (configs[2])",
+    "arch": "Qwen2.5-0.5B: 24 layers, hidden 896, 14q/2kv heads x 64, SwiGLU 4864, vocab 151936 tied",
+    "n_prompt": N_PROMPT, "n_gen": N_GEN, "batch": 1, "max_ctx": MAX_CTX,
+    "weights": "random-init N(0,0.02) fp16 in the reference file layout (990,162,688 B)",
+    "l2": "no flush: 988 MB of weights streamed per token > 126 MB L2",
+}
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+RANK, WORLD, LOCAL_RANK = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def weights_path():
+    d = "/dev/shm/sb200_bench" if os.path.isdir("/dev/shm") else "/tmp/sb200_bench"
+    os.makedirs(d, exist_ok=True)
+    return os.path.join(d, f"qwen_{WEIGHT_SEED}.bin")
+
+
+def ensure_weights(barrier):
+    import sb200
+    path = weights_path()
+    if LOCAL_RANK == 0 and not (os.path.exists(path) and os.path.getsize(path) == sb200.QWEN["FILE_BYTES"]):
+        tmp = path + f".tmp{os.getpid()}"
+        sb200.synth_weights(sb200.MODEL_QWEN, tmp, WEIGHT_SEED)
+        os.replace(tmp, path)
+    barrier()
+    return path
+
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gpu_index():
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ent = vis.split(",")
+        if LOCAL_RANK < len(ent) and ent[LOCAL_RANK].strip().isdigit():
+            return int(ent[LOCAL_RANK])
+    return LOCAL_RANK
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the step kernels from the committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# ------------------------------------------------------------------ CPU legs
+def ref_bench_exe():
+    exe = os.path.join(REPO, "oracle", "_ref", "ref_qwen_bench")
+    return exe if os.access(exe, os.X_OK) else None
+
+
+def run_ref_bench(path, procs, warmup, steps, tokens):
+    exe = ref_bench_exe()
+    out = subprocess.run([exe, path, str(procs), str(warmup), str(steps), str(tokens), "42"],
+                         capture_output=True, text=True, timeout=1800)
+    if out.returncode != 0:
+        raise RuntimeError(f"ref_qwen_bench failed: {out.stderr[-400:]}")
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def cpu_baseline(path):
+    """Reference CPU decode on this host's cores, bounded sample (rank 0, N=1)."""
+    cores = host_cores()
+    if ref_bench_exe():
+        r = run_ref_bench(path, cores, 0, 1, 2)
+        return {"value": round(r["tok_s"], 4), "unit": UNIT, "cores": cores, "kind": "reference",
+                "sample": f"{cores} forked replicas of the reference cpu_forward (qwen_engine.c:292-358) + argmax, "
+                          f"2 greedy decode tokens each; {r['timed_s']:.1f} s wall"}
+    # oracle restatement (row-parallel threads) when the reference build is absent
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    import numpy as np
+    import orc
+    m = orc.Model("qwen", path, 8, 151936)
+    m.forward(42, 0, True)
+    t0 = time.perf_counter()
+    tok = 42
+    for p in range(1, 3):
+        tok = int(np.argmax(m.forward(tok, p, True, nthreads=cores)))
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": round(2 / dt, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": "oracle restatement of cpu_forward, rows split over threads, 2 decode tokens"}
+
+
+def run_reference_arm(args):
+    if RANK != 0:
+        return
+    line = {"impl": "reference", "metric": METRIC, "unit": UNIT, "higher_is_better": True}
+    if not ref_bench_exe():
+        line["unavailable"] = "oracle/_ref/ref_qwen_bench not built (needs the reference sources at build time)"
+        print(json.dumps(line))
+        return
+    import sb200  # noqa: F401  (synthetic weight writer)
+    path = ensure_weights(lambda: None)
+    cores = host_cores()
+    r = run_ref_bench(path, cores, args.warmup, args.steps, 2)
+    step_ms = 1e3 * r["timed_s"] / r["steps"]
+    line.update({
+        "value": round(r["tok_s"], 4), "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 3), "scaling": "weak", "vs_baseline": None, "dtype": "f16w-f32",
+        "data": "synthetic", "config": dict(CONFIG, impl="reference CPU (single-threaded engine, one replica per core)"),
+        "cpu_baseline": {"value": round(r["tok_s"], 4), "unit": UNIT, "cores": cores, "kind": "reference",
+                         "sample": f"per step: {cores} replicas x 2 greedy decode tokens of the reference cpu_forward"},
+        "e2e": {"value": round(r["tok_s"], 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    })
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_b200(args):
+    import torch
+    import sb200
+
+    dist = WORLD > 1
+    if dist:
+        import datetime
+        import torch.distributed as tdist
+        torch.cuda.set_device(LOCAL_RANK)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", LOCAL_RANK))
+
+        def barrier():
+            tdist.barrier()
+    else:
+        def barrier():
+            pass
+    dev = torch.device("cuda", LOCAL_RANK)
+    torch.cuda.set_device(dev)
+    torch.zeros(1, device=dev)
+    sb200.init(LOCAL_RANK)
+    path = ensure_weights(barrier)
+
+    eng = sb200.Engine(sb200.MODEL_QWEN, path, MAX_CTX)
+    ext = torch.cuda.ExternalStream(eng.stream, device=dev)
+    prompt = sb200.synth_ids(N_PROMPT, sb200.QWEN["V"], 1000 + RANK)
+
+    def decode_step():
+        """One request with resident inputs: returns decode-loop ms (events)."""
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        eng.begin(prompt, N_GEN)
+        eng.steps(N_PROMPT - 1, False)  # prompt tokens, no LM head
+        eng.steps(1, True)  # last prompt token -> first generated token
+        e0.record(ext)
+        eng.steps(N_GEN, True)  # the 256 timed decode steps
+        e1.record(ext)
+        ids = eng.finish(N_PROMPT + N_GEN + 1)
+        assert len(ids) == N_PROMPT + N_GEN + 1
+        return e0.elapsed_time(e1)
+
+    for _ in range(args.warmup):
+        decode_step()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = Clocks(gpu_index())
+    if RANK == 0:
+        clocks.start()
+        time.sleep(0.3)
+    t_wall0 = time.perf_counter()
+    ms = [decode_step() for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t_wall0
+    clk = clocks.stop() if RANK == 0 else None
+    barrier()
+    total = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+    if dist:
+        import torch.distributed as tdist
+        tdist.all_reduce(total, op=tdist.ReduceOp.MAX)
+    total_ms = float(total.item())
+    value = WORLD * args.steps * N_GEN / (total_ms / 1e3)
+
+    # ---- e2e through the public C-ABI call, host (pinned) buffers
+    pin_in = torch.tensor(prompt, dtype=torch.int32).pin_memory()
+    pin_out = torch.zeros(N_PROMPT + N_GEN + 1, dtype=torch.int32).pin_memory()
+    import ctypes
+    L = sb200.lib()
+    nout = ctypes.c_int()
+
+    def e2e_step():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        sb200.check(L.sb_engine_generate(eng.h, ctypes.c_void_p(pin_in.data_ptr()), N_PROMPT, N_GEN,
+                                         ctypes.c_void_p(pin_out.data_ptr()), ctypes.byref(nout), 0))
+        e1.record(ext)
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    barrier()
+    e2e_ms = [e2e_step() for _ in range(args.steps)]
+    e2e_total = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
+    if dist:
+        import torch.distributed as tdist
+        tdist.all_reduce(e2e_total, op=tdist.ReduceOp.MAX)
+    e2e_value = WORLD * args.steps * N_GEN / (float(e2e_total.item()) / 1e3)
+
+    # ---- roofline of the dominant kernel (standalone, L2 flushed before each launch)
+    peaks = measured_peaks()
+    peak = float(peaks["hbm_gbs"]) if peaks and peaks.get("hbm_gbs") else FALLBACK_HBM_GBS
+    peak_src = "measured" if peaks and peaks.get("hbm_gbs") else "fallback"
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    prof = {}
+    for name, kid, per_step in (("qwen_gateup_swiglu", eng.K_MLP_UP, 24), ("qwen_lmhead", eng.K_LMHEAD, 1),
+                                ("qwen_gemv_resid(down)", eng.K_MLP_DOWN, 24), ("qwen_qkv_rope", eng.K_QKV, 24),
+                                ("qwen_gemv_resid(o)", eng.K_O, 24)):
+        kms, kbytes = eng.profile(kid, 20, flush, flush.numel())
+        prof[name] = {"ms": kms, "bytes": kbytes, "per_step": per_step, "gbs": kbytes / (kms * 1e-3) / 1e9}
+    dom = max(prof, key=lambda k: prof[k]["ms"] * prof[k]["per_step"])
+    d = prof[dom]
+    traffic = ncu_traffic().get(dom)
+    roofline = {"kernel": dom, "bound": "hbm", "achieved": round(d["gbs"], 1), "peak": peak, "unit": "GB/s",
+                "frac": round(d["gbs"] / peak, 4), "traffic": traffic, "peak_source": peak_src,
+                "bytes_per_launch": d["bytes"], "launch_us": round(d["ms"] * 1e3, 2),
+                "step_frac": round(eng.step_bytes() * (value / WORLD) / 1e9 / peak, 4),
+                "kernels": {k: {"GB/s": round(v["gbs"], 1), "us": round(v["ms"] * 1e3, 2)} for k, v in prof.items()}}
+    del flush
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": WORLD, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": round(value / BASELINE_TOKS, 1), "dtype": "f16w-f32", "data": "synthetic",
+        "config": dict(CONFIG, global_batch=WORLD, seq_len=N_PROMPT + N_GEN,
+                       parallelism=f"replicas x{WORLD} (decode does not shard)"),
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": N_PROMPT * 4 + 48,
+                "d2h_bytes_per_step": (N_PROMPT + N_GEN + 1) * 4 + 48,
+                "note": "sb_engine_generate: prompt from pinned host memory, prefill 32 + decode 256, ids back"},
+        "gpu_launches": args.steps * N_GEN * eng.launches_per_step(True),
+        "roofline": roofline,
+        "clocks": clk,
+        "wall_s_timed": round(wall, 3),
+    }
+    eng.close()
+    if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = cpu_baseline(path)
+        except Exception as ex:  # reported, not fatal
+            line["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+    if RANK == 0:
+        print(json.dumps(line))
+    if dist:
+        import torch.distributed as tdist
+        barrier()
+        tdist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

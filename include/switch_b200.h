@@ -1,0 +1,175 @@
+/* switch_b200.h -- C-ABI of the B200 (sm_100a) matrix-multiply hot path of
+ * pkia/switch-l4t-gpu.
+ *
+ * Two boundaries are provided.
+ *
+ * 1. Module images (the reference's own boundary).  libswitch_b200.so ships
+ *    four cubins whose `extern "C" __global__` kernels keep the reference's
+ *    names and parameter lists, so a reference host that does
+ *    cuModuleLoadData + cuModuleGetFunction + cuLaunchKernel (void** params,
+ *    its hard-coded grids) works unchanged with them:
+ *      switch_gpu.cubin  sgemm_tiled, sgemm_tiled4, sgemm_opt, sgemm_naive,
+ *                        membw_read4                 (switch_gpu.cu:5-152)
+ *      gemv.cubin        gemv, gemv4, gemv_warp      (gpu-llm/kernels/gemv.cu)
+ *      gpt2.cubin        gemv_warp, gemv_warp_b, gemv_multi, layernorm, gelu,
+ *                        add_bias, add2, attn_scores, attn_softmax, attn_mix
+ *                                                    (gpt2_kernels.cu:38-268)
+ *      qwen.cubin        gemv_h, rmsnorm, rope, swiglu, attn_scores_gqa,
+ *                        attn_softmax, attn_mix_gqa, add2
+ *                                                    (qwen_kernels.cu:34-189)
+ *    sb_module_image() returns them for hosts that load from memory.
+ *
+ * 2. Host entry points (below): the launches the reference's C hosts make,
+ *    as plain C functions with device pointers, sizes and a CUstream
+ *    (passed as void*; NULL = the legacy default stream).  They use the
+ *    CUDA driver API on the calling thread's current context; when none is
+ *    current, device 0's primary context is retained and made current (the
+ *    context the CUDA runtime, NCCL and PyTorch also use).
+ *
+ * Errors: every function returns 0 on success, else a nonzero CUresult (or
+ * SB_ERR_* below) and records a message for sb_last_error().  Nothing
+ * exits the process (the reference hosts' CHK macro does; cuda_drv.h:39-40).
+ * Kernels never allocate; the caller owns every buffer, as in the reference.
+ */
+#ifndef SWITCH_B200_H
+#define SWITCH_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_ERR_ARG 9001    /* invalid argument (size, alignment, null)    */
+#define SB_ERR_FILE 9002   /* weight file missing or of the wrong size    */
+#define SB_ERR_STATE 9003  /* engine not ready / misuse                   */
+
+/* ---- runtime ------------------------------------------------------------ */
+/* Make a context current (device `device`'s primary context if none is) and
+ * load the module images into it.  Called implicitly by every entry point. */
+int sb_init(int device);
+/* Message of the last failure on this thread ("" if none). */
+const char *sb_last_error(void);
+/* Embedded module image by name ("switch_gpu", "gemv", "gpt2", "qwen"):
+ * pointer/size of the sm_100a cubin, for cuModuleLoadData. */
+int sb_module_image(const char *name, const void **image, size_t *size);
+/* SM count of the current device. */
+int sb_sm_count(void);
+
+/* ---- SGEMM (replaces the launches of gpu_workload.c:90,135,142,160,168,186)
+ * C[M][N] = A[M][K] . B[K][N], FP32 row-major, FP32 FFMA on CUDA cores.
+ * Any M, N, K >= 0; 128-bit loads when K, N % 4 == 0 and pointers aligned. */
+int sb_sgemm(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
+/* Rows [row0, row1) of C only: the row panel a rank computes when C is
+ * sharded across GPUs (A, C point at the full matrices). */
+int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
+                  void *stream);
+
+/* ---- bandwidth probe (membw_read4, gpu_workload.c:197-220) ---------------
+ * out[i] (i < min(n4, grid*block)) = sum of this thread's float4s, `iters`
+ * passes over buf[n4]; grid = 0 picks 4 CTAs per SM. */
+int sb_membw_read4(const void *buf, float *out, int n4, int iters, int grid, void *stream);
+/* FP32 FMA probe: returns the FLOP count issued (grid*256*iters*256). */
+int sb_fma_peak(float *out, int iters, int grid, void *stream, double *flops);
+
+/* ---- GEMV ------------------------------------------------------------------
+ * y[n] = sum_k W[n][k] x[k] (+ bias[n] if bias), W row-major [N][K].
+ * FP32 weights: gemv / gemv4 / gemv_warp / gemv_warp_b (gemv.cu:3-71,
+ * gpt2_kernels.cu:38-108).  K % 4 == 0. */
+int sb_gemv_f32(const float *W, const float *x, const float *bias, float *y, int K, int N, void *stream);
+/* Y[t][n] = sum_k W[n][k] X[t][k] (+ bias[n]) for T token rows
+ * (gemv_multi, gpt2_kernels.cu:115-155). */
+int sb_gemv_multi_f32(const float *W, const float *X, const float *bias, float *Y, int K, int N, int T,
+                      void *stream);
+/* FP16 weights (raw IEEE half bits, exponent-0 values read as 0 as in the
+ * reference's h2f), FP32 x, y, bias: gemv_h (qwen_kernels.cu:34-70).
+ * K % 8 == 0. */
+int sb_gemv_h(const uint16_t *W, const float *x, const float *bias, float *y, int K, int N, void *stream);
+/* FP16 weights and FP16 activations, batch B in 1..8: Y[b][n] =
+ * sum_k h2f(W[n][k]) h2f(X[b][k]), FP32 accumulate and output (the GEMV
+ * sweep's y = W x with x FP16).  K % 8 == 0. */
+int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
+
+/* ---- decode-step pieces (Qwen2.5 FP16-weight path, qwen_engine.c:205-269)
+ * Exposed for kernel-level parity tests; the engines below fuse them.      */
+int sb_rmsnorm(const float *x, const uint16_t *w, float *y, int n, float eps, int rows, void *stream);
+int sb_rope(float *x, const float *cosT, const float *sinT, int T, int H, int HD, int pos0, void *stream);
+int sb_swiglu(const float *g, const float *u, float *y, int n, void *stream);
+/* Decode attention of one query token over cached positions [0, T):
+ * out[h*HD+d] = sum_t softmax_t(scale q_h.k_t) v_t[g*HD+d], g = h/(NH/NKV).
+ * kc/vc rows have stride kv_stride floats.  HD must be 64, NH/NKV in {1,7}.
+ * part: >= NKV*ceil(T/16)*(NH/NKV)*66 floats; counters: NKV zeroed uints
+ * (left zeroed on return).  Replaces attn_scores_gqa/attn_softmax/
+ * attn_mix_gqa (qwen_kernels.cu:130-180) and attn_scores/attn_softmax/
+ * attn_mix (gpt2_kernels.cu:221-268). */
+int sb_attn_decode(const float *q, const float *kc, const float *vc, float *out, int T, int NH, int NKV,
+                   int HD, int kv_stride, float scale, float *part, unsigned *counters, void *stream);
+int sb_layernorm(const float *x, const float *w, const float *b, float *y, int n, float eps, int rows,
+                 void *stream);
+int sb_gelu(const float *x, float *y, int n, void *stream);
+
+/* ---- engines ---------------------------------------------------------------
+ * One process, one model, one GPU.  Weight files use the reference's exact
+ * flat layouts (qwen_engine.c:8-16,60-75 / conv_qwen.py; gpt2_engine.c:10-13,
+ * 50-70 / conv_gpt2.py).  The whole decode step runs on the device: token
+ * embedding, all layers, final norm, LM head, argmax and the next-token
+ * write, captured once as a CUDA graph and replayed per token. */
+typedef struct sb_engine sb_engine;
+#define SB_MODEL_QWEN 1
+#define SB_MODEL_GPT2 2
+#define SB_FLAG_NO_GRAPH 1u  /* launch kernels directly instead of graph replay */
+#define SB_FLAG_NO_PDL 2u    /* no programmatic dependent launch            */
+#define SB_GEN_STOP_EOS 1u   /* stop at the model's end tokens (reference behaviour) */
+
+/* max_ctx: KV-cache positions (<= 8192 Qwen, <= 1024 GPT-2). NULL on error. */
+sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, unsigned flags);
+void sb_engine_destroy(sb_engine *e);
+int sb_engine_reset(sb_engine *e); /* zero the KV cache */
+/* One decode step with the reference's gpu_forward contract
+ * (qwen_engine.c:205 / gpt2_engine.c:174): token at pos, cache gains pos;
+ * when want_logits, the V logits are computed and, if logits_host != NULL,
+ * copied there (synchronous). */
+int sb_engine_forward(sb_engine *e, int token, int pos, int want_logits, float *logits_host);
+/* Greedy generation: prompt ids from host memory, then n_gen+1 tokens are
+ * produced exactly as the reference's prime-then-generate loop
+ * (qwen_engine.c:523-548).  out_ids receives prompt + generated ids (room
+ * for n_prompt+n_gen+1); returns the count in *n_out. */
+int sb_engine_generate(sb_engine *e, const int *prompt, int n_prompt, int n_gen, int *out_ids, int *n_out,
+                       unsigned gen_flags);
+/* The same, split so a caller can time the phases on sb_engine_stream():
+ * begin = upload prompt/state; steps = n graph replays (prefill steps use
+ * with_logits=0); finish = synchronise and copy ids back. */
+int sb_engine_begin(sb_engine *e, const int *prompt, int n_prompt, int n_gen, unsigned gen_flags);
+int sb_engine_steps(sb_engine *e, int n, int with_logits);
+int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out);
+void *sb_engine_stream(sb_engine *e);
+/* Device pointer of the logits buffer (V floats) and the vocabulary size. */
+int sb_engine_logits(sb_engine *e, const float **dev_logits, int *vocab);
+/* Kernel launches issued per decode step (with / without LM head). */
+int sb_engine_launches_per_step(sb_engine *e, int with_logits);
+/* Bytes of weights a decode step streams (with LM head). */
+double sb_engine_step_bytes(sb_engine *e);
+/* Time `reps` standalone launches (CUDA events on the engine stream) of one
+ * kernel of the step -- 1 QKV, 2 attention, 3 O-proj, 4 MLP up (gate|up or
+ * fc), 5 MLP down, 6 LM head (layer 0 where it applies) -- each after an
+ * optional memset of `flush` (an L2-sized device buffer) so weights come
+ * from HBM.  Reports the average ms and the kernel's algorithmic bytes. */
+int sb_engine_profile(sb_engine *e, int which, int reps, void *flush, size_t flush_bytes, float *avg_ms,
+                      double *bytes);
+
+/* ---- synthetic inputs in the reference layouts -----------------------------
+ * Deterministic from `seed`: weights N(0, 0.02) (fp16 round-to-nearest for
+ * Qwen), norm gains 1, LN betas 0, biases N(0, 0.02); Qwen RoPE tables
+ * theta 1e6 as conv_qwen.py:75-80.  Returns bytes written. */
+long sb_synth_weights(int model, const char *path, uint64_t seed);
+/* n ids uniform in [0, vocab). */
+void sb_synth_ids(int *ids, int n, int vocab, uint64_t seed);
+/* n floats uniform in [lo, hi). */
+void sb_synth_uniform(float *out, size_t n, float lo, float hi, uint64_t seed);
+/* n fp16 values N(0, std), round-to-nearest-even. */
+void sb_synth_normal_h(uint16_t *out, size_t n, float stdv, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

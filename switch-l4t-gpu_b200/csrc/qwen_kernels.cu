@@ -1,0 +1,417 @@
+// qwen_kernels.cu -- the "qwen" module image (sm_100a cubin).
+//
+// Part 1: drop-in kernels with the reference's exact names and parameter
+// lists (gpu-llm/kernels/qwen_kernels.cu), correct under the launch geometry
+// the reference host hard-codes (qwen_engine.c:216-265) or any other.
+// Part 2: fused decode-step kernels used by this package's engine; they take
+// the step position from device memory so one captured CUDA graph replays
+// every token, and they use programmatic dependent launch so each kernel's
+// weight prefetch overlaps its predecessor's tail.
+#include "sb_attn.cuh"
+#include "sb_gemv.cuh"
+
+// =====================================================================
+// Part 1 -- drop-ins
+// =====================================================================
+
+// y[n] = sum_k h2f(W[n*K+k]) * x[k] (+ bias[n]).  Reference:
+// qwen_kernels.cu:34-70 (grid ceil(N/8), block 256).  Warp-per-row-task,
+// grid-stride over all warps, so any grid works; fp16 flush-to-zero decode.
+extern "C" __global__ void gemv_h(const unsigned short *__restrict__ W, const float *__restrict__ x,
+                                  const float *__restrict__ bias, float *__restrict__ y, int K, int N) {
+    const int nthreads = gridDim.x * blockDim.x;
+    const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool vec = ((K & 7) == 0) && ((((uintptr_t)W) & 15) == 0) && ((((uintptr_t)x) & 15) == 0);
+    if (vec && (blockDim.x & 31) == 0) {
+        const int warp = gtid >> 5, nwarp = nthreads >> 5;
+        const int cpr = K >> 3;
+        XGlob8 xa{x};
+        for (int n = warp; n < N; n += nwarp) {
+            float acc[1];
+            const int rows[1] = {n};
+            warp_dot_h<1, 4>(reinterpret_cast<const uint4 *>(W), cpr, rows, cpr, xa, acc);
+            if ((threadIdx.x & 31) == 0) y[n] = acc[0] + (bias ? bias[n] : 0.0f);
+        }
+        return;
+    }
+    // K % 8 != 0 (the reference only needs K % 4 == 0) or odd block shape:
+    // one thread per row, still exact fp16 decode.
+    for (int n = gtid; n < N; n += nthreads) {
+        const unsigned short *row = W + (size_t)n * K;
+        float acc = 0.0f;
+        for (int k = 0; k < K; k++) acc = fmaf(h2f_ftz(row[k]), x[k], acc);
+        y[n] = acc + (bias ? bias[n] : 0.0f);
+    }
+}
+
+// y = x * rsqrt(mean(x^2) + eps) * h2f(w); one block per row (grid = T).
+// Reference: qwen_kernels.cu:74-93.
+extern "C" __global__ void rmsnorm(const float *__restrict__ x, const unsigned short *__restrict__ w,
+                                   float *__restrict__ y, int n, float eps) {
+    __shared__ float red[32];
+    x += (size_t)blockIdx.x * n;
+    y += (size_t)blockIdx.x * n;
+    const float inv = block_rms_scale(x, n, eps, red);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], inv), h2f_ftz(w[i]));
+}
+
+// Half-split RoPE from cos/sin tables; one thread per (t, head, pair).
+// Reference: qwen_kernels.cu:97-116.  Products and the difference are
+// rounded separately, as the reference's C computes them.
+extern "C" __global__ void rope(float *__restrict__ x, const float *__restrict__ cosT,
+                                const float *__restrict__ sinT, int T, int H, int HD, int pos0) {
+    const int hd2 = HD / 2;
+    const long total = (long)T * H * hd2;
+    for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(idx / (H * hd2));
+        const int r = (int)(idx % (H * hd2));
+        const int h = r / hd2, i = r % hd2;
+        float *row = x + (size_t)t * H * HD;
+        const float a = row[h * HD + i], b = row[h * HD + hd2 + i];
+        const float c = cosT[(size_t)(pos0 + t) * hd2 + i], s = sinT[(size_t)(pos0 + t) * hd2 + i];
+        row[h * HD + i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        row[h * HD + hd2 + i] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+}
+
+SB_DEV float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// y = silu(g) * u.  Reference: qwen_kernels.cu:119-126.
+extern "C" __global__ void swiglu(const float *__restrict__ g, const float *__restrict__ u,
+                                  float *__restrict__ y, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        y[i] = silu_mul(g[i], u[i]);
+}
+
+// scores[t*NH+h] = scale * q_h . kc[t*KV + g*HD ..], g = h / (NH/(KV/HD)).
+// Reference: qwen_kernels.cu:130-144 (one thread per (t, h)).
+extern "C" __global__ void attn_scores_gqa(const float *__restrict__ q, const float *__restrict__ kc,
+                                           float *__restrict__ scores, int T, float scale, int NH,
+                                           int KV, int HD) {
+    const int grp = NH / (KV / HD);
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < T * NH; idx += gridDim.x * blockDim.x) {
+        const int t = idx / NH, h = idx % NH, g = h / grp;
+        const float *qp = q + h * HD;
+        const float *kp = kc + (size_t)t * KV + g * HD;
+        float acc = 0.0f;
+        for (int d = 0; d < HD; d++) acc = fmaf(qp[d], kp[d], acc);
+        scores[idx] = acc * scale;
+    }
+}
+
+// Per-head softmax over T (the stock host launches NH threads).
+// Reference: qwen_kernels.cu:147-164.
+extern "C" __global__ void attn_softmax(const float *__restrict__ scores, float *__restrict__ probs,
+                                        int T, int NH) {
+    for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < NH; h += gridDim.x * blockDim.x) {
+        float maxv = -1e30f;
+        for (int t = 0; t < T; t++) maxv = fmaxf(maxv, scores[(size_t)t * NH + h]);
+        float sum = 0.0f;
+        for (int t = 0; t < T; t++) {
+            float e = expf(scores[(size_t)t * NH + h] - maxv);
+            probs[(size_t)t * NH + h] = e;
+            sum += e;
+        }
+        const float inv = 1.0f / sum;
+        for (int t = 0; t < T; t++) probs[(size_t)t * NH + h] *= inv;
+    }
+}
+
+// out[h*HD+d] = sum_t probs[t*NH+h] * vc[t*KV + g*HD + d].
+// Reference: qwen_kernels.cu:167-180.
+extern "C" __global__ void attn_mix_gqa(const float *__restrict__ probs, const float *__restrict__ vc,
+                                        float *__restrict__ out, int T, int NH, int KV, int HD) {
+    const int grp = NH / (KV / HD);
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < NH * HD; idx += gridDim.x * blockDim.x) {
+        const int h = idx / HD, d = idx % HD, g = h / grp;
+        float acc = 0.0f;
+        for (int t = 0; t < T; t++) acc = fmaf(probs[(size_t)t * NH + h], vc[(size_t)t * KV + g * HD + d], acc);
+        out[idx] = acc;
+    }
+}
+
+// out = a + b.  Reference: qwen_kernels.cu:183-189.
+extern "C" __global__ void add2(const float *__restrict__ a, const float *__restrict__ b,
+                                float *__restrict__ out, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        out[i] = a[i] + b[i];
+}
+
+// =====================================================================
+// Part 1b -- this package's standalone entry kernels (tuned geometry)
+// =====================================================================
+
+// y = W x (+bias) with x staged once per CTA in shared memory and 4-row
+// warp tasks; a contiguous row range per CTA.  Launched by sb_gemv_h with
+// grid ~ 4 CTAs/SM, block 256, dynamic smem K*4.  K % 8 == 0.
+extern "C" __global__ void __launch_bounds__(256) gemv_h_b200(const unsigned short *__restrict__ W,
+                                                              const float *__restrict__ x,
+                                                              const float *__restrict__ bias,
+                                                              float *__restrict__ y, int K, int N) {
+    extern __shared__ float4 xs4[];
+    constexpr int R = 4;
+    int t0, t1;
+    cta_task_range((N + R - 1) / R, t0, t1);
+    float4 *lo = xs4, *hi = xs4 + K / 8;
+    stage_x_split8(x, K, lo, hi, 1.0f, nullptr);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, cpr = K / 8, lane = threadIdx.x & 31;
+    XSplit8 xa{lo, hi};
+    for (int t = t0 + warp; t < t1; t += nw) {
+        int rows[R];
+        consecutive_rows<R>(t * R, N, rows);
+        float acc[R];
+        warp_dot_h<R, 4>(reinterpret_cast<const uint4 *>(W), cpr, rows, cpr, xa, acc);
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            if (lane == r && rows[r] >= 0) y[rows[r]] = acc[r] + (bias ? bias[rows[r]] : 0.0f);
+    }
+}
+
+// Y[b][n] = sum_k h2f(W[n][k]) h2f(X[b][k]) for B activation rows (fp16,
+// decoded with the same flush-to-zero rule), FP32 out.  dynamic smem
+// B*K*4.  K % 8 == 0.
+template <int B>
+__device__ void gemv_hh_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
+                             float *__restrict__ Y, int K, int N) {
+    extern __shared__ float4 xsb[];
+    constexpr int R = 4;
+    int t0, t1;
+    cta_task_range((N + R - 1) / R, t0, t1);
+    const int cpr = K / 8;
+    float4 *lo = xsb, *hi = xsb + B * cpr;
+    for (int i = threadIdx.x; i < B * cpr; i += blockDim.x) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(X + (size_t)i * 8);
+        const float2 f0 = h2x2_ftz(w.x), f1 = h2x2_ftz(w.y), f2 = h2x2_ftz(w.z), f3 = h2x2_ftz(w.w);
+        lo[i] = make_float4(f0.x, f0.y, f1.x, f1.y);
+        hi[i] = make_float4(f2.x, f2.y, f3.x, f3.y);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int t = t0 + warp; t < t1; t += nw) {
+        int rows[R];
+        consecutive_rows<R>(t * R, N, rows);
+        float acc[R][B];
+        warp_dot_hb<R, (B > 2 ? 2 : 4), B>(reinterpret_cast<const uint4 *>(W), cpr, rows, cpr, lo, hi, acc);
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int b = 0; b < B; b++)
+                if (lane == r * B + b && rows[r] >= 0) Y[(size_t)b * N + rows[r]] = acc[r][b];
+    }
+}
+extern "C" __global__ void __launch_bounds__(256) gemv_hh1(const unsigned short *W, const unsigned short *X,
+                                                           float *Y, int K, int N) {
+    gemv_hh_body<1>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemv_hh2(const unsigned short *W, const unsigned short *X,
+                                                           float *Y, int K, int N) {
+    gemv_hh_body<2>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemv_hh4(const unsigned short *W, const unsigned short *X,
+                                                           float *Y, int K, int N) {
+    gemv_hh_body<4>(W, X, Y, K, N);
+}
+
+// GQA decode attention with an explicit T (no step state); 7 query heads
+// per KV head.  grid (NKV, max_splits), block SB_ATTN_THREADS.
+extern "C" __global__ void attn_decode_g7(const float *__restrict__ q, const float *__restrict__ kc,
+                                          const float *__restrict__ vc, int T, float *__restrict__ out,
+                                          float *__restrict__ part, unsigned *__restrict__ counters,
+                                          int kv_stride, float scale, int max_splits) {
+    attn_decode_body<7>(q, kc, vc, T, out, part, counters, kv_stride, scale, max_splits);
+}
+
+// =====================================================================
+// Part 2 -- fused decode-step kernels (this package's engine)
+// =====================================================================
+#include "sb_step.h"
+#include "sb_finalize.cuh"
+#include "sb_resid.cuh"
+
+// x = h2f(emb[tokens[pos]]): the embedding gather the reference does on the
+// host each token (qwen_engine.c:207-211).
+extern "C" __global__ void qwen_embed(const unsigned short *__restrict__ emb, const int *__restrict__ tokens,
+                                      SbStep *__restrict__ st, float *__restrict__ x, int C) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (sb_step_idle(st)) return;
+    const int tok = tokens[st->pos];
+    const unsigned short *row = emb + (size_t)tok * C;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) x[i] = h2f_ftz(row[i]);
+}
+
+// RMSNorm(x) -> QKV GEMV (+bias) -> RoPE(q, k) -> q out, k/v straight into
+// the KV cache at `pos`.  Replaces rmsnorm + gemv_h + 2x rope + 2 DtoD copies
+// of qwen_engine.c:216-230.  A warp owns the RoPE pair rows (i, i+HD/2) of
+// one head, so the rotation happens in its epilogue.
+// grid: any; block: multiple of 32; dynamic smem: C * 4 bytes.
+extern "C" __global__ void qwen_qkv_rope(const unsigned short *__restrict__ Wqkv,
+                                         const unsigned short *__restrict__ bqkv,
+                                         const unsigned short *__restrict__ g_in,
+                                         const float *__restrict__ x, const float *__restrict__ cosT,
+                                         const float *__restrict__ sinT, SbStep *__restrict__ st,
+                                         float *__restrict__ q_out, float *__restrict__ kc,
+                                         float *__restrict__ vc, int C, int NH, int NKV, int HD, float eps) {
+    extern __shared__ float4 xs4[];
+    __shared__ float red[32];
+    const int KVD = NKV * HD, NQKV = C + 2 * KVD, hd2 = HD / 2;
+    const int ntasks = NQKV / 2;  // (head, i) pairs
+    int t0, t1;
+    cta_task_range(ntasks, t0, t1);
+    pdl_launch_dependents();
+    if (threadIdx.x == 0 && t1 > t0) {
+        for (int h = t0 / hd2; h <= (t1 - 1) / hd2; h++) {
+            const int i0 = max(t0 - h * hd2, 0), i1 = min(t1 - h * hd2, hd2);
+            prefetch_rows(Wqkv, (long)C * 2, h * HD + i0, h * HD + i1, 1L << 20);
+            prefetch_rows(Wqkv, (long)C * 2, h * HD + hd2 + i0, h * HD + hd2 + i1, 1L << 20);
+        }
+    }
+    pdl_wait();
+    if (sb_step_idle(st)) return;
+    const int pos = st->pos;
+    const float inv = block_rms_scale(x, C, eps, red);
+    float4 *lo = xs4, *hi = xs4 + C / 8;
+    stage_x_split8(x, C, lo, hi, inv, g_in);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int cpr = C / 8;
+    XSplit8 xa{lo, hi};
+    for (int t = t0 + warp; t < t1; t += nw) {
+        const int h = t / hd2, i = t % hd2;
+        const int rows[2] = {h * HD + i, h * HD + hd2 + i};
+        float a[2];
+        warp_dot_h<2, 4>(reinterpret_cast<const uint4 *>(Wqkv), cpr, rows, cpr, xa, a);
+        if ((threadIdx.x & 31) == 0) {
+            float y0 = __fadd_rn(a[0], h2f_ftz(bqkv[rows[0]]));
+            float y1 = __fadd_rn(a[1], h2f_ftz(bqkv[rows[1]]));
+            if (h < NH + NKV) {  // q and k heads are rotated
+                const float c = cosT[(size_t)pos * hd2 + i], s = sinT[(size_t)pos * hd2 + i];
+                const float o0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, s));
+                const float o1 = __fadd_rn(__fmul_rn(y0, s), __fmul_rn(y1, c));
+                y0 = o0;
+                y1 = o1;
+            }
+            if (h < NH) {
+                q_out[rows[0]] = y0;
+                q_out[rows[1]] = y1;
+            } else if (h < NH + NKV) {
+                kc[(size_t)pos * KVD + (rows[0] - C)] = y0;
+                kc[(size_t)pos * KVD + (rows[1] - C)] = y1;
+            } else {
+                vc[(size_t)pos * KVD + (rows[0] - C - KVD)] = y0;
+                vc[(size_t)pos * KVD + (rows[1] - C - KVD)] = y1;
+            }
+        }
+    }
+}
+
+// GQA decode attention at the step's position.  grid (NKV, max_splits),
+// block SB_ATTN_THREADS.  Replaces attn_scores_gqa + attn_softmax +
+// attn_mix_gqa (qwen_engine.c:231-236).  part/counters are scratch owned by
+// the caller: (NKV*max_splits*7*66) floats and NKV zeroed counters.
+extern "C" __global__ void qwen_attn(const float *__restrict__ q, const float *__restrict__ kc,
+                                     const float *__restrict__ vc, SbStep *__restrict__ st,
+                                     float *__restrict__ out, float *__restrict__ part,
+                                     unsigned *__restrict__ counters, int kv_stride, float scale,
+                                     int max_splits) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (sb_step_idle(st)) return;
+    attn_decode_body<7>(q, kc, vc, st->pos + 1, out, part, counters, kv_stride, scale, max_splits);
+}
+
+// x[n] += sum_k h2f(W[n][k]) v[k]: the O and down projections with the
+// residual add fused (replaces gemv_h + add2, qwen_engine.c:242-245,256-259);
+// each row split over `ksplit` warps.  grid: any; block: multiple of 32 with
+// (block/32) % ksplit == 0; no dynamic smem.
+extern "C" __global__ void qwen_gemv_resid(const unsigned short *__restrict__ W, const float *__restrict__ v,
+                                           SbStep *__restrict__ st, float *__restrict__ x, int K, int N,
+                                           int ksplit) {
+    resid_splitk_body<true>(W, nullptr, v, st, x, K, N, ksplit);
+}
+
+// RMSNorm(x) -> gate|up GEMV -> SwiGLU: hid[i] = silu(g_i) * u_i; a warp owns
+// gate rows (i, i+1) and up rows (FC+i, FC+i+1).  Replaces rmsnorm + gemv_h
+// + swiglu (qwen_engine.c:247-254).  dynamic smem: C * 4 bytes.
+extern "C" __global__ void qwen_gateup_swiglu(const unsigned short *__restrict__ Wgu,
+                                              const unsigned short *__restrict__ g_post,
+                                              const float *__restrict__ x, SbStep *__restrict__ st,
+                                              float *__restrict__ hid, int C, int FC, float eps) {
+    extern __shared__ float4 xs4[];
+    __shared__ float red[32];
+    int t0, t1;
+    cta_task_range((FC + 1) / 2, t0, t1);
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        const long r0 = 2L * t0, r1 = min(2L * t1, (long)FC);
+        prefetch_rows(Wgu, (long)C * 2, r0, r1, 1L << 20);
+        prefetch_rows(Wgu, (long)C * 2, FC + r0, FC + r1, 1L << 20);
+    }
+    pdl_wait();
+    if (sb_step_idle(st)) return;
+    const float inv = block_rms_scale(x, C, eps, red);
+    float4 *lo = xs4, *hi = xs4 + C / 8;
+    stage_x_split8(x, C, lo, hi, inv, g_post);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, cpr = C / 8;
+    XSplit8 xa{lo, hi};
+    for (int t = t0 + warp; t < t1; t += nw) {
+        const int i = 2 * t;
+        const bool two = (i + 1 < FC);
+        const int rows[4] = {i, two ? i + 1 : -1, FC + i, two ? FC + i + 1 : -1};
+        float a[4];
+        warp_dot_h<4, 4>(reinterpret_cast<const uint4 *>(Wgu), cpr, rows, cpr, xa, a);
+        const int lane = threadIdx.x & 31;
+        if (lane == 0) hid[i] = silu_mul(a[0], a[2]);
+        if (lane == 1 && two) hid[i + 1] = silu_mul(a[1], a[3]);
+    }
+}
+
+// Final RMSNorm -> tied LM head GEMV (logits) -> argmax, fused.  Replaces
+// rmsnorm + gemv_h + the host argmax over V logits (qwen_engine.c:263-268,
+// 360-364).  dynamic smem: C * 4 bytes.
+extern "C" __global__ void qwen_lmhead(const unsigned short *__restrict__ Wemb,
+                                       const unsigned short *__restrict__ g_final,
+                                       const float *__restrict__ x, SbStep *__restrict__ st,
+                                       float *__restrict__ logits, int C, int V, float eps) {
+    extern __shared__ float4 xs4[];
+    __shared__ float red[32];
+    __shared__ unsigned long long best_s;
+    constexpr int R = 4;
+    int t0, t1;
+    cta_task_range((V + R - 1) / R, t0, t1);
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) prefetch_rows(Wemb, (long)C * 2, (long)t0 * R, min((long)t1 * R, (long)V), 96L << 10);
+    pdl_wait();
+    if (sb_step_idle(st)) return;
+    if (threadIdx.x == 0) best_s = 0ull;
+    const float inv = block_rms_scale(x, C, eps, red);
+    float4 *lo = xs4, *hi = xs4 + C / 8;
+    stage_x_split8(x, C, lo, hi, inv, g_final);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, cpr = C / 8, lane = threadIdx.x & 31;
+    XSplit8 xa{lo, hi};
+    unsigned long long best = 0ull;
+    for (int t = t0 + warp; t < t1; t += nw) {
+        int rows[R];
+        consecutive_rows<R>(t * R, V, rows);
+        float acc[R];
+        warp_dot_h<R, 4>(reinterpret_cast<const uint4 *>(Wemb), cpr, rows, cpr, xa, acc);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            if (rows[r] >= 0) {
+                if (lane == r) logits[rows[r]] = acc[r];
+                const unsigned long long k = argmax_key(acc[r], rows[r]);
+                best = k > best ? k : best;
+            }
+        }
+    }
+    if (lane == 0 && best) atomicMax(&best_s, best);
+    __syncthreads();
+    if (threadIdx.x == 0 && best_s) atomicMax(&st->key, best_s);
+}
+

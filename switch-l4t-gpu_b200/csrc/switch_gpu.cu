@@ -1,0 +1,269 @@
+// switch_gpu.cu -- the "switch_gpu" module image (sm_100a cubin): the SGEMM
+// family and the bandwidth probe with the reference's names and parameter
+// lists (switch_gpu.cu of pkia/switch-l4t-gpu), plus this package's own
+// entry points.
+//
+// SGEMM design (FP32 CUDA cores; B200 has no FP32 tensor path):
+//   * 128x128 CTA tile, BK-deep k-slices, 256 threads, 8x8 outputs per
+//     thread as 2x2 blocks of 4x4 (rows ty*4 and 64+ty*4, cols tx*4 and
+//     64+tx*4).  A warp covers 4 (ty) x 8 (tx) threads, so each 128-bit
+//     fragment load from shared memory touches 4 or 8 distinct 16-byte words:
+//     one wavefront, broadcast to the other lanes.
+//   * A is stored k-major (transposed) in shared memory; its 16-byte units
+//     are XOR-swizzled by k (unit ^ 2*(k/4)) so the transposing 32-bit stores
+//     of a warp hit 32 distinct banks while fragment reads stay 128-bit.
+//     B is stored as loaded.  Two shared buffers: the next k-slice is fetched into
+//     registers while the current one is multiplied, then stored into the
+//     other buffer -- one __syncthreads per slice.
+//   * Tiles are walked by a grid-stride loop over a grouped (8 tile-rows)
+//     order, so ANY grid shape is correct -- the stock harness launches
+//     (n/32)^2 or (n/64)^2 CTAs of 16x16 threads (gpu_workload.c:90,142,168)
+//     and no dynamic shared memory (all 33 KB here are static).
+//   * Edges are predicated (zero-filled loads, guarded stores), so M, N, K
+//     need not be multiples of anything; 128-bit global loads are used when
+//     K and N are multiples of 4 and the pointers are 16-byte aligned.
+#include "sb_common.cuh"
+
+#define SG_BM 128
+#define SG_BN 128
+#define SG_BK 16
+#define SG_THREADS 256
+
+struct SgSmem {
+    float As[2][SG_BK][SG_BM];  // k-major, 16-byte units swizzled by sg_swz(k)
+    float Bs[2][SG_BK][SG_BN];
+};
+__device__ __forceinline__ int sg_swz(int k) { return (k >> 2) << 1; }
+
+template <bool VEC>
+__device__ __forceinline__ void sg_load_slice(const float *__restrict__ A, const float *__restrict__ B, int M,
+                                              int N, int K, int m0, int n0, int k0, int tid, float4 (&ra)[2],
+                                              float4 (&rb)[2]) {
+    // A slice: 128 rows x 16 k = 512 float4; thread loads rows tid>>2 and
+    // 64+(tid>>2), k-quad (tid&3)*4.
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int r = m0 + h * 64 + (tid >> 2), c = k0 + (tid & 3) * 4;
+        if (VEC) {
+            ra[h] = (r < M && c < K) ? __ldg(reinterpret_cast<const float4 *>(A + (size_t)r * K + c))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            const float *p = A + (size_t)r * K;
+            ra[h].x = (r < M && c + 0 < K) ? p[c + 0] : 0.f;
+            ra[h].y = (r < M && c + 1 < K) ? p[c + 1] : 0.f;
+            ra[h].z = (r < M && c + 2 < K) ? p[c + 2] : 0.f;
+            ra[h].w = (r < M && c + 3 < K) ? p[c + 3] : 0.f;
+        }
+    }
+    // B slice: 16 k-rows x 128 cols = 512 float4; thread loads k-rows
+    // tid>>5 and 8+(tid>>5), col quad (tid&31)*4.
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int r = k0 + h * 8 + (tid >> 5), c = n0 + (tid & 31) * 4;
+        if (VEC) {
+            rb[h] = (r < K && c < N) ? __ldg(reinterpret_cast<const float4 *>(B + (size_t)r * N + c))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            const float *p = B + (size_t)r * N;
+            rb[h].x = (r < K && c + 0 < N) ? p[c + 0] : 0.f;
+            rb[h].y = (r < K && c + 1 < N) ? p[c + 1] : 0.f;
+            rb[h].z = (r < K && c + 2 < N) ? p[c + 2] : 0.f;
+            rb[h].w = (r < K && c + 3 < N) ? p[c + 3] : 0.f;
+        }
+    }
+}
+
+__device__ __forceinline__ void sg_store_slice(SgSmem &s, int buf, int tid, const float4 (&ra)[2],
+                                               const float4 (&rb)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int m = h * 64 + (tid >> 2), k = (tid & 3) * 4;
+        const int ms = (((m >> 2) ^ sg_swz(k)) << 2) | (m & 3);  // same swizzle for k..k+3
+        s.As[buf][k + 0][ms] = ra[h].x;
+        s.As[buf][k + 1][ms] = ra[h].y;
+        s.As[buf][k + 2][ms] = ra[h].z;
+        s.As[buf][k + 3][ms] = ra[h].w;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+        *reinterpret_cast<float4 *>(&s.Bs[buf][h * 8 + (tid >> 5)][(tid & 31) * 4]) = rb[h];
+}
+
+template <bool VEC>
+__device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const float *__restrict__ B,
+                                            float *__restrict__ C, int M, int N, int K, int tid, int cta,
+                                            int ncta, SgSmem &s) {
+    const int warp = tid >> 5, lane = tid & 31;
+    const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15
+    const int tx = (warp & 1) * 8 + (lane & 7);    // 0..15
+    const int tiles_m = (M + SG_BM - 1) / SG_BM, tiles_n = (N + SG_BN - 1) / SG_BN;
+    const int ntiles = tiles_m * tiles_n;
+    const int nk = (K + SG_BK - 1) / SG_BK;
+    const bool cvec = ((N & 3) == 0) && ((((uintptr_t)C) & 15) == 0);
+
+    for (int tile = cta; tile < ntiles; tile += ncta) {
+        // grouped raster: 8 tile-rows share the B column panels in L2
+        const int per_group = 8 * tiles_n;
+        const int first_m = (tile / per_group) * 8;
+        const int gsz = min(tiles_m - first_m, 8);
+        const int tm = first_m + (tile % per_group) % gsz;
+        const int tn = (tile % per_group) / gsz;
+        const int m0 = tm * SG_BM, n0 = tn * SG_BN;
+
+        float acc[8][8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+
+        float4 ra[2], rb[2];
+        sg_load_slice<VEC>(A, B, M, N, K, m0, n0, 0, tid, ra, rb);
+        __syncthreads();  // previous tile's readers are done with buffer 0
+        sg_store_slice(s, 0, tid, ra, rb);
+        __syncthreads();
+        for (int kt = 0; kt < nk; kt++) {
+            const int buf = kt & 1;
+            if (kt + 1 < nk) sg_load_slice<VEC>(A, B, M, N, K, m0, n0, (kt + 1) * SG_BK, tid, ra, rb);
+#pragma unroll
+            for (int k = 0; k < SG_BK; k++) {
+                const float4 a0 = *reinterpret_cast<const float4 *>(&s.As[buf][k][(ty ^ sg_swz(k)) * 4]);
+                const float4 a1 = *reinterpret_cast<const float4 *>(&s.As[buf][k][((16 + ty) ^ sg_swz(k)) * 4]);
+                const float4 b0 = *reinterpret_cast<const float4 *>(&s.Bs[buf][k][tx * 4]);
+                const float4 b1 = *reinterpret_cast<const float4 *>(&s.Bs[buf][k][64 + tx * 4]);
+                const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+            }
+            if (kt + 1 < nk) sg_store_slice(s, buf ^ 1, tid, ra, rb);
+            __syncthreads();
+        }
+        // epilogue
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
+            if (r >= M) continue;
+#pragma unroll
+            for (int hb = 0; hb < 2; hb++) {
+                const int c = n0 + hb * 64 + tx * 4;
+                float *p = C + (size_t)r * N + c;
+                if (cvec && c + 3 < N) {
+                    *reinterpret_cast<float4 *>(p) =
+                        make_float4(acc[i][hb * 4 + 0], acc[i][hb * 4 + 1], acc[i][hb * 4 + 2], acc[i][hb * 4 + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (c + j < N) p[j] = acc[i][hb * 4 + j];
+                }
+            }
+        }
+    }
+}
+
+// Any-shape fallback for launches whose block is not 256 threads: each
+// thread computes whole outputs.
+__device__ void sgemm_any(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M,
+                          int N, int K) {
+    const long nthreads = (long)gridDim.x * gridDim.y * gridDim.z * blockDim.x * blockDim.y * blockDim.z;
+    const long cta = (blockIdx.z * gridDim.y + blockIdx.y) * (long)gridDim.x + blockIdx.x;
+    const long tid = cta * blockDim.x * blockDim.y * blockDim.z +
+                     (threadIdx.z * blockDim.y + threadIdx.y) * blockDim.x + threadIdx.x;
+    for (long o = tid; o < (long)M * N; o += nthreads) {
+        const int i = (int)(o / N), j = (int)(o % N);
+        float acc = 0.0f;
+        for (int k = 0; k < K; k++) acc = fmaf(A[(size_t)i * K + k], B[(size_t)k * N + j], acc);
+        C[o] = acc;
+    }
+}
+
+__device__ __forceinline__ void sgemm_entry(const float *A, const float *B, float *C, int M, int N, int K) {
+    const int nth = blockDim.x * blockDim.y * blockDim.z;
+    if (nth != SG_THREADS) { sgemm_any(A, B, C, M, N, K); return; }
+    const int tid = (threadIdx.z * blockDim.y + threadIdx.y) * blockDim.x + threadIdx.x;
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    const int ncta = gridDim.x * gridDim.y * gridDim.z;
+    const bool vec = ((K & 3) == 0) && ((N & 3) == 0) && ((((uintptr_t)A) & 15) == 0) &&
+                     ((((uintptr_t)B) & 15) == 0);
+    __shared__ __align__(16) SgSmem s;
+    if (vec) sgemm_tiles<true>(A, B, C, M, N, K, tid, cta, ncta, s);
+    else sgemm_tiles<false>(A, B, C, M, N, K, tid, cta, ncta, s);
+}
+
+// Reference: switch_gpu.cu:5-39 (stock launch: grid (n/32, n/32), block 16x16).
+extern "C" __global__ void __launch_bounds__(256, 1)
+    sgemm_tiled(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
+    sgemm_entry(A, B, C, M, N, K);
+}
+// Reference: switch_gpu.cu:59-95 (stock launch: grid (n/64, n/64), block 16x16).
+extern "C" __global__ void __launch_bounds__(256, 1)
+    sgemm_tiled4(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
+    sgemm_entry(A, B, C, M, N, K);
+}
+// Reference: switch_gpu.cu:99-137 (stock launch: grid (n/64, n/64), block 16x16).
+extern "C" __global__ void __launch_bounds__(256, 1)
+    sgemm_opt(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
+    sgemm_entry(A, B, C, M, N, K);
+}
+// This package's launch of the same kernel body: grid = min(tiles, 2*SMs),
+// block 256 (issued by sb_sgemm).
+extern "C" __global__ void __launch_bounds__(256, 1)
+    sgemm_b200(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
+    sgemm_entry(A, B, C, M, N, K);
+}
+
+// One output per thread, k in order, product and sum rounded separately:
+// the same float arithmetic as the harness's CPU loop (gpu_workload.c:97-98),
+// so its result is bit-identical to it.  Reference: switch_gpu.cu:140-152
+// (grid (n/16, n/16), block 16x16); grid-strided here so any grid works.
+extern "C" __global__ void sgemm_naive(const float *__restrict__ A, const float *__restrict__ B,
+                                       float *__restrict__ C, int M, int N, int K) {
+    for (int row = blockIdx.y * blockDim.y + threadIdx.y; row < M; row += gridDim.y * blockDim.y)
+        for (int col = blockIdx.x * blockDim.x + threadIdx.x; col < N; col += gridDim.x * blockDim.x) {
+            float acc = 0.0f;
+            for (int k = 0; k < K; k++) acc = __fadd_rn(acc, __fmul_rn(A[(size_t)row * K + k], B[(size_t)k * N + col]));
+            C[(size_t)row * N + col] = acc;
+        }
+}
+
+// Streaming read: out[i0] = sum over this thread's float4s of (x+y+z+w),
+// `iters` passes.  Reference: switch_gpu.cu:41-54 (grid 512, block 256).
+// Four independent 128-bit loads per thread are kept in flight.
+extern "C" __global__ void membw_read4(const float4 *__restrict__ buf, float *__restrict__ out, int n4, int iters) {
+    const long i0 = threadIdx.x + (long)blockIdx.x * blockDim.x;
+    const long stride = (long)gridDim.x * blockDim.x;
+    float acc = 0.f;
+    for (int it = 0; it < iters; ++it) {
+        long i = i0;
+        for (; i + 3 * stride < n4; i += 4 * stride) {
+            const float4 v0 = __ldcs(buf + i), v1 = __ldcs(buf + i + stride);
+            const float4 v2 = __ldcs(buf + i + 2 * stride), v3 = __ldcs(buf + i + 3 * stride);
+            acc += v0.x + v0.y + v0.z + v0.w;
+            acc += v1.x + v1.y + v1.z + v1.w;
+            acc += v2.x + v2.y + v2.z + v2.w;
+            acc += v3.x + v3.y + v3.z + v3.w;
+        }
+        for (; i < n4; i += stride) {
+            const float4 v = __ldcs(buf + i);
+            acc += v.x + v.y + v.z + v.w;
+        }
+    }
+    if (i0 < n4) out[i0] = acc;
+}
+
+// FP32 FMA throughput probe (the B200 counterpart of the reference's
+// hand-PTX fma_bench, gpu_test.c:63-79): 8 independent FMA chains per
+// thread, `iters` x 8 x 2 FLOP per thread.
+extern "C" __global__ void fma_peak(float *__restrict__ out, int iters, float m, float c) {
+    float a0 = threadIdx.x * 1e-3f, a1 = a0 + 1.f, a2 = a0 + 2.f, a3 = a0 + 3.f;
+    float a4 = a0 + 4.f, a5 = a0 + 5.f, a6 = a0 + 6.f, a7 = a0 + 7.f;
+    for (int i = 0; i < iters; i++) {
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+            a0 = fmaf(a0, m, c); a1 = fmaf(a1, m, c); a2 = fmaf(a2, m, c); a3 = fmaf(a3, m, c);
+            a4 = fmaf(a4, m, c); a5 = fmaf(a5, m, c); a6 = fmaf(a6, m, c); a7 = fmaf(a7, m, c);
+        }
+    }
+    out[blockIdx.x * blockDim.x + threadIdx.x] = a0 + a1 + a2 + a3 + a4 + a5 + a6 + a7;
+}

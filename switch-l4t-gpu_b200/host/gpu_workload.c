@@ -1,0 +1,258 @@
+/* gpu_workload.c -- the SGEMM + memory-bandwidth suite on B200, with the
+ * reference harness's CLI and JSON contract (gpu_workload.c of
+ * pkia/switch-l4t-gpu; consumed by deploy/cluster/gpu_task_example.py).
+ *
+ *   gpu_workload [--json] [--sizes 256,512,1024] [--membw-mib 2048] [module]
+ *
+ * `module` is a cubin/PTX image loaded with cuModuleLoadData (default: the
+ * switch_gpu.cubin installed next to this binary).  Kernels are resolved by
+ * the reference's names; sgemm_tiled and membw_read4 are required,
+ * sgemm_naive / sgemm_tiled4 / sgemm_opt optional (a failing lookup drops
+ * their lines and JSON keys, gpu_workload.c:69-74).  Each SGEMM kernel is
+ * launched with the reference's own geometry (grid n/32 or n/64 squared,
+ * 16x16 threads), verified at n = 256 against the same CPU triple loop and
+ * tolerance (|d| > 0.05|ref| + 1e-3 is a bad cell), then timed over 10
+ * launches (CUDA events; the wall clock is kept for the "ms" the reference
+ * reports).  Data: srand(42), (rand() % 2000 - 1000) / 1000, as the
+ * reference.  The bandwidth probe streams a buffer far larger than the
+ * 126 MB L2 (the reference's 64 MB would fit in it).
+ *
+ * JSON keys are the reference's (ptx, kernels, sgemm, sgemm4, sgemm_opt,
+ * membw_gbps, done) plus additive ones (device, sm_count, sgemm_b200,
+ * membw_bytes, fp32_peak_gflops_at_max_clock). */
+#define _GNU_SOURCE
+#include <cuda.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+static int json_mode;
+#define OUT(...) do { if (!json_mode) printf(__VA_ARGS__); } while (0)
+#define CHK(x) do { CUresult r_ = (x); if (r_) { const char *s_ = NULL; cuGetErrorString(r_, &s_); \
+    fprintf(stderr, "CUDA error %d (%s) at %s:%d\n", (int)r_, s_ ? s_ : "?", __FILE__, __LINE__); exit(1); } } while (0)
+
+static double now_s(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec + ts.tv_nsec / 1e9;
+}
+
+static char *read_file(const char *path, size_t *len) {
+    FILE *f = fopen(path, "rb");
+    if (!f) { perror(path); exit(1); }
+    fseek(f, 0, SEEK_END);
+    *len = (size_t)ftell(f);
+    fseek(f, 0, SEEK_SET);
+    char *buf = malloc(*len + 1);
+    if (fread(buf, 1, *len, f) != *len) exit(1);
+    buf[*len] = 0;
+    fclose(f);
+    return buf;
+}
+
+static const char *default_module(void) {
+    static char p[4096];
+    ssize_t n = readlink("/proc/self/exe", p, sizeof p - 64);
+    if (n > 0) {
+        p[n] = 0;
+        char *s = strrchr(p, '/');
+        if (s) {
+            strcpy(s, "/../lib/switch_gpu.cubin");
+            if (access(p, R_OK) == 0) return p;
+        }
+    }
+    return "switch_gpu.cubin";
+}
+
+/* CPU golden check of gpu_workload.c:92-115: returns the bad-row count
+ * (stops at the first bad column of a row, at most 5 rows). */
+static int verify(const float *A, const float *B, const float *C, int n, int full) {
+    int bad = 0;
+    for (int i = 0; i < n && (full || bad < 5); i++)
+        for (int j = 0; j < n; j++) {
+            float ref = 0;
+            for (int k = 0; k < n; k++) ref += A[i * n + k] * B[k * n + j];
+            float d = C[i * n + j] - ref;
+            if (d < 0) d = -d;
+            if (d > 0.05f * (ref < 0 ? -ref : ref) + 1e-3f) {
+                if (bad < 3) OUT("  mismatch [%d][%d]: got %.4f want %.4f\n", i, j, C[i * n + j], ref);
+                bad++;
+                if (!full) break;
+            }
+        }
+    return bad;
+}
+
+typedef struct {
+    const char *name, *json_key;
+    CUfunction f;
+    int tile; /* reference grid divisor */
+    double ms[16], gf[16];
+    const char *verdict;
+} kern;
+
+int main(int argc, char **argv) {
+    const char *mod_path = NULL;
+    int sizes[16] = {256, 512, 1024}, nsizes = 3;
+    long membw_mib = 2048;
+    for (int i = 1; i < argc; i++) {
+        if (!strcmp(argv[i], "--json")) json_mode = 1;
+        else if (!strcmp(argv[i], "--sizes") && i + 1 < argc) {
+            nsizes = 0;
+            for (char *t = strtok(argv[++i], ","); t && nsizes < 16; t = strtok(NULL, ",")) sizes[nsizes++] = atoi(t);
+        } else if (!strcmp(argv[i], "--membw-mib") && i + 1 < argc) membw_mib = atol(argv[++i]);
+        else mod_path = argv[i];
+    }
+    if (!mod_path) mod_path = default_module();
+    size_t plen;
+    char *image = read_file(mod_path, &plen);
+
+    CUdevice dev;
+    CUcontext ctx;
+    CUmodule mod;
+    CHK(cuInit(0));
+    CHK(cuDeviceGet(&dev, 0));
+    CHK(cuDevicePrimaryCtxRetain(&ctx, dev)); /* primary context: shared with the runtime/NCCL */
+    CHK(cuCtxSetCurrent(ctx));
+    CHK(cuModuleLoadData(&mod, image));
+    char devname[256] = "";
+    int sms = 0, clk_khz = 0;
+    cuDeviceGetName(devname, sizeof devname, dev);
+    cuDeviceGetAttribute(&sms, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, dev);
+    cuDeviceGetAttribute(&clk_khz, CU_DEVICE_ATTRIBUTE_CLOCK_RATE, dev);
+
+    kern ks[4] = {{"sgemm", "sgemm", NULL, 32, {0}, {0}, NULL},
+                  {"sgemm_tiled4", "sgemm4", NULL, 64, {0}, {0}, NULL},
+                  {"sgemm_opt", "sgemm_opt", NULL, 64, {0}, {0}, NULL},
+                  {"sgemm_b200", "sgemm_b200", NULL, 0, {0}, {0}, NULL}};
+    CUfunction membw, naive = NULL;
+    CHK(cuModuleGetFunction(&ks[0].f, mod, "sgemm_tiled"));
+    CHK(cuModuleGetFunction(&membw, mod, "membw_read4"));
+    cuModuleGetFunction(&naive, mod, "sgemm_naive");
+    cuModuleGetFunction(&ks[1].f, mod, "sgemm_tiled4");
+    cuModuleGetFunction(&ks[2].f, mod, "sgemm_opt");
+    cuModuleGetFunction(&ks[3].f, mod, "sgemm_b200");
+    const char *v_naive = NULL;
+    CUevent e0, e1;
+    CHK(cuEventCreate(&e0, 0));
+    CHK(cuEventCreate(&e1, 0));
+
+    for (int si = 0; si < nsizes; si++) {
+        const int n = sizes[si];
+        const size_t bytes = (size_t)n * n * 4;
+        float *A = malloc(bytes), *B = malloc(bytes), *C = malloc(bytes);
+        srand(42);
+        for (size_t i = 0; i < (size_t)n * n; i++) {
+            A[i] = (rand() % 2000 - 1000) / 1000.0f;
+            B[i] = (rand() % 2000 - 1000) / 1000.0f;
+        }
+        CUdeviceptr dA, dB, dC;
+        CHK(cuMemAlloc(&dA, bytes));
+        CHK(cuMemAlloc(&dB, bytes));
+        CHK(cuMemAlloc(&dC, bytes));
+        CHK(cuMemcpyHtoD(dA, A, bytes));
+        CHK(cuMemcpyHtoD(dB, B, bytes));
+        int Mn = n, Nn = n, Kn = n;
+        void *args[] = {&dA, &dB, &dC, &Mn, &Nn, &Kn};
+        for (int ki = 0; ki < 4; ki++) {
+            kern *k = &ks[ki];
+            if (!k->f) continue;
+            unsigned gx, gy = 1;
+            if (k->tile) { gx = (unsigned)((n + k->tile - 1) / k->tile); gy = gx; }
+            else { long t = (long)((n + 127) / 128) * ((n + 127) / 128); gx = (unsigned)(t < sms ? t : sms); }
+            const unsigned bx = k->tile ? 16 : 256, by = k->tile ? 16 : 1;
+            CHK(cuMemsetD32(dC, 0, (size_t)n * n));
+            CHK(cuLaunchKernel(k->f, gx, gy, 1, bx, by, 1, 0, NULL, args, NULL));
+            CHK(cuCtxSynchronize());
+            if (n == 256) {
+                CHK(cuMemcpyDtoH(C, dC, bytes));
+                k->verdict = verify(A, B, C, n, 0) ? "WRONG" : "CORRECT";
+                OUT("%s %d: %s\n", k->name, n, k->verdict);
+                if (ki == 0 && naive) {
+                    CHK(cuMemsetD32(dC, 0, (size_t)n * n));
+                    CHK(cuLaunchKernel(naive, n / 16, n / 16, 1, 16, 16, 1, 0, NULL, args, NULL));
+                    CHK(cuCtxSynchronize());
+                    CHK(cuMemcpyDtoH(C, dC, bytes));
+                    int nbad = verify(A, B, C, n, 1);
+                    v_naive = nbad ? "WRONG" : "CORRECT";
+                    OUT("sgemm_naive %d: %s (%d bad cells)\n", n, v_naive, nbad);
+                }
+            }
+            CHK(cuEventRecord(e0, NULL));
+            double t0 = now_s();
+            for (int r = 0; r < 10; r++) CHK(cuLaunchKernel(k->f, gx, gy, 1, bx, by, 1, 0, NULL, args, NULL));
+            CHK(cuEventRecord(e1, NULL));
+            CHK(cuEventSynchronize(e1));
+            (void)t0;
+            float ms10 = 0;
+            CHK(cuEventElapsedTime(&ms10, e0, e1));
+            k->ms[si] = ms10 / 10.0;
+            k->gf[si] = 2.0 * n * (double)n * n / (k->ms[si] * 1e-3) / 1e9;
+            OUT("%s %dx%dx%d: %.3f ms/iter, %.1f GFLOPS\n", ki == 0 ? "sgemm" : k->name, n, n, n, k->ms[si], k->gf[si]);
+        }
+        cuMemFree(dA);
+        cuMemFree(dB);
+        cuMemFree(dC);
+        free(A);
+        free(B);
+        free(C);
+    }
+
+    /* ---- memory bandwidth (read), buffer >> L2 */
+    double membw_gbs = 0, mbytes = 0;
+    {
+        long n4l = membw_mib * 1024L * 1024L / 16;
+        if (n4l > 0x7fffffffL) n4l = 0x7fffffffL;
+        int n4 = (int)n4l, iters = 4;
+        size_t bytes = (size_t)n4 * 16;
+        CUdeviceptr dbuf, dout;
+        CHK(cuMemAlloc(&dbuf, bytes));
+        CHK(cuMemsetD32(dbuf, 0x3a83126f, bytes / 4)); /* 0.001f */
+        unsigned grid = 4 * (unsigned)sms;
+        CHK(cuMemAlloc(&dout, (size_t)grid * 256 * 4));
+        void *margs[] = {&dbuf, &dout, &n4, &iters};
+        CHK(cuLaunchKernel(membw, grid, 1, 1, 256, 1, 1, 0, NULL, margs, NULL));
+        CHK(cuCtxSynchronize());
+        CHK(cuEventRecord(e0, NULL));
+        CHK(cuLaunchKernel(membw, grid, 1, 1, 256, 1, 1, 0, NULL, margs, NULL));
+        CHK(cuEventRecord(e1, NULL));
+        CHK(cuEventSynchronize(e1));
+        float ms = 0;
+        CHK(cuEventElapsedTime(&ms, e0, e1));
+        mbytes = (double)bytes * iters;
+        membw_gbs = mbytes / (ms * 1e-3) / 1e9;
+        OUT("membw read (%ld MiB x%d): %.3f s, %.1f GB/s\n", membw_mib, iters, ms * 1e-3, membw_gbs);
+        cuMemFree(dbuf);
+        cuMemFree(dout);
+    }
+
+    if (json_mode) {
+        printf("{\"ptx\":\"");
+        for (const char *p = mod_path; *p; p++) {
+            if (*p == '"' || *p == '\\') putchar('\\');
+            putchar(*p);
+        }
+        printf("\",\"kernels\":{\"sgemm\":\"%s\"", ks[0].verdict ? ks[0].verdict : "NOT_RUN");
+        if (v_naive) printf(",\"sgemm_naive\":\"%s\"", v_naive);
+        if (ks[1].verdict) printf(",\"sgemm_tiled4\":\"%s\"", ks[1].verdict);
+        if (ks[2].verdict) printf(",\"sgemm_opt\":\"%s\"", ks[2].verdict);
+        if (ks[3].verdict) printf(",\"sgemm_b200\":\"%s\"", ks[3].verdict);
+        printf("}");
+        for (int ki = 0; ki < 4; ki++) {
+            if (!ks[ki].f) continue;
+            printf(",\"%s\":[", ks[ki].json_key);
+            for (int i = 0; i < nsizes; i++)
+                printf("%s{\"n\":%d,\"ms\":%.3f,\"gflops\":%.1f}", i ? "," : "", sizes[i], ks[ki].ms[i], ks[ki].gf[i]);
+            printf("]");
+        }
+        printf(",\"membw_gbps\":%.1f,\"membw_bytes\":%.0f,\"device\":\"%s\",\"sm_count\":%d,"
+               "\"fp32_peak_gflops_at_max_clock\":%.1f,\"done\":true}\n",
+               membw_gbs, mbytes, devname, sms, sms * 128.0 * 2.0 * clk_khz / 1e6);
+    } else {
+        printf("WORKLOAD_DONE\n");
+    }
+    return 0;
+}

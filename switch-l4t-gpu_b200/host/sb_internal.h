@@ -1,0 +1,75 @@
+/* sb_internal.h -- private declarations of libswitch_b200 (driver-API host). */
+#ifndef SB_INTERNAL_H
+#define SB_INTERNAL_H
+#include <cuda.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/switch_b200.h"
+
+enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_COUNT };
+
+typedef enum {
+    F_SGEMM_B200 = 0,
+    F_SGEMM_NAIVE,
+    F_MEMBW,
+    F_FMA_PEAK,
+    F_GEMV_F32_B200,
+    F_GEMV_MULTI,
+    F_LAYERNORM,
+    F_GELU,
+    F_ATTN_G1,
+    F_GPT2_EMBED,
+    F_GPT2_LN_QKV,
+    F_GPT2_ATTN,
+    F_GPT2_RESID,
+    F_GPT2_LN_FC,
+    F_GPT2_LMHEAD,
+    F_GPT2_FINALIZE,
+    F_GEMV_H_B200,
+    F_GEMV_HH1,
+    F_GEMV_HH2,
+    F_GEMV_HH4,
+    F_RMSNORM,
+    F_ROPE,
+    F_SWIGLU,
+    F_ATTN_G7,
+    F_QWEN_EMBED,
+    F_QWEN_QKV,
+    F_QWEN_ATTN,
+    F_QWEN_RESID,
+    F_QWEN_GATEUP,
+    F_QWEN_LMHEAD,
+    F_QWEN_FINALIZE,
+    F_COUNT
+} sb_fn_id;
+
+typedef struct sb_ctx {
+    CUcontext ctx;
+    CUdevice dev;
+    CUmodule mod[M_COUNT];
+    CUfunction fn[F_COUNT];
+    int smem_set[F_COUNT]; /* dynamic smem limit already raised to this */
+    int sms;
+} sb_ctx;
+
+/* error reporting (thread-local message) */
+int sb_fail(int code, const char *what, const char *file, int line);
+#define SB_CK(call)                                                           \
+    do {                                                                      \
+        CUresult r_ = (call);                                                 \
+        if (r_ != CUDA_SUCCESS) return sb_fail((int)r_, #call, __FILE__, __LINE__); \
+    } while (0)
+#define SB_ARG(cond, msg)                                                     \
+    do {                                                                      \
+        if (!(cond)) return sb_fail(SB_ERR_ARG, msg, __FILE__, __LINE__);     \
+    } while (0)
+
+/* current-context state (modules loaded); NULL on failure (error recorded) */
+sb_ctx *sb_ctx_get(void);
+/* launch fn with grid/block/dynamic smem on stream; pdl != 0 adds the
+ * programmatic stream-serialisation attribute */
+int sb_launch(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned bx, unsigned smem, CUstream s,
+              void **args, int pdl);
+
+#endif

@@ -1,0 +1,190 @@
+/* sb_ops.c -- host entry points for the individual hot-path operations.
+ * Each one validates its arguments, picks the launch shape for this device
+ * and issues one (or a few) kernel launches on the caller's stream. */
+#include <stdint.h>
+
+#include "sb_internal.h"
+
+#define CEIL_DIV(a, b) (((a) + (b)-1) / (b))
+#define DP(p) ((CUdeviceptr)(uintptr_t)(p))
+#define ALIGNED16(p) ((((uintptr_t)(p)) & 15) == 0)
+
+static int occupancy(sb_ctx *c, sb_fn_id f, int block, size_t smem) {
+    int n = 1;
+    /* resolve the function through a zero-size launch */
+    if (sb_launch(c, f, 0, 0, block, 0, NULL, NULL, 0)) return 1;
+    if (cuOccupancyMaxActiveBlocksPerMultiprocessor(&n, c->fn[f], block, smem) != CUDA_SUCCESS || n < 1) n = 1;
+    return n;
+}
+
+/* ------------------------------------------------------------------ SGEMM */
+int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
+                  void *stream) {
+    SB_ARG(M >= 0 && N >= 0 && K >= 0 && 0 <= row0 && row0 <= row1 && row1 <= M, "bad SGEMM shape");
+    SB_ARG(A && B && C, "null pointer");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    const int m = row1 - row0;
+    if (m == 0 || N == 0) return 0;
+    CUdeviceptr a = DP(A + (size_t)row0 * K), b = DP(B), cc = DP(C + (size_t)row0 * N);
+    const long tiles = (long)CEIL_DIV(m, 128) * CEIL_DIV(N, 128);
+    static __thread int occ = 0;
+    if (!occ) occ = occupancy(c, F_SGEMM_B200, 256, 0);
+    long grid = tiles < (long)c->sms * occ ? tiles : (long)c->sms * occ;
+    void *args[] = {&a, &b, &cc, (void *)&m, &N, &K};
+    return sb_launch(c, F_SGEMM_B200, (unsigned)grid, 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+int sb_sgemm(const float *A, const float *B, float *C, int M, int N, int K, void *stream) {
+    return sb_sgemm_rows(A, B, C, M, N, K, 0, M, stream);
+}
+
+/* ------------------------------------------------------------------ probes */
+int sb_membw_read4(const void *buf, float *out, int n4, int iters, int grid, void *stream) {
+    SB_ARG(buf && out && n4 >= 0 && iters >= 0 && ALIGNED16(buf), "bad membw arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (grid <= 0) grid = 4 * c->sms;
+    CUdeviceptr b = DP(buf), o = DP(out);
+    void *args[] = {&b, &o, &n4, &iters};
+    return sb_launch(c, F_MEMBW, (unsigned)grid, 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+int sb_fma_peak(float *out, int iters, int grid, void *stream, double *flops) {
+    SB_ARG(out && iters > 0, "bad fma_peak arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (grid <= 0) grid = 8 * c->sms;
+    CUdeviceptr o = DP(out);
+    float m = 0.999999f, a = 1e-6f;
+    void *args[] = {&o, &iters, &m, &a};
+    if (flops) *flops = (double)grid * 256.0 * iters * 16.0 * 8.0 * 2.0;
+    return sb_launch(c, F_FMA_PEAK, (unsigned)grid, 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+/* ------------------------------------------------------------------ GEMV */
+static unsigned gemv_grid(sb_ctx *c, long tasks, int warps) {
+    long g = CEIL_DIV(tasks, warps);
+    long cap = 4L * c->sms;
+    if (g > cap) g = cap;
+    return (unsigned)(g < 1 ? 1 : g);
+}
+
+int sb_gemv_f32(const float *W, const float *x, const float *bias, float *y, int K, int N, void *stream) {
+    SB_ARG(W && x && y && K > 0 && N >= 0, "bad GEMV arguments");
+    SB_ARG(K % 4 == 0 && ALIGNED16(W) && ALIGNED16(x), "gemv_f32 needs K % 4 == 0 and 16-byte aligned W, x");
+    SB_ARG((size_t)K * 4 <= 200 * 1024, "gemv_f32: K too large for the shared x stage");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr w = DP(W), xx = DP(x), b = DP(bias), yy = DP(y);
+    void *args[] = {&w, &xx, &b, &yy, &K, &N};
+    return sb_launch(c, F_GEMV_F32_B200, gemv_grid(c, CEIL_DIV(N, 4), 8), 1, 256, (unsigned)K * 4,
+                     (CUstream)stream, args, 0);
+}
+
+int sb_gemv_multi_f32(const float *W, const float *X, const float *bias, float *Y, int K, int N, int T,
+                      void *stream) {
+    SB_ARG(W && X && Y && K > 0 && N >= 0 && T >= 0, "bad gemv_multi arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr w = DP(W), xx = DP(X), b = DP(bias), yy = DP(Y);
+    void *args[] = {&w, &xx, &b, &yy, &K, &N, &T};
+    return sb_launch(c, F_GEMV_MULTI, (unsigned)CEIL_DIV(N, 8), (unsigned)CEIL_DIV(T, 16), 256, 0,
+                     (CUstream)stream, args, 0);
+}
+
+int sb_gemv_h(const uint16_t *W, const float *x, const float *bias, float *y, int K, int N, void *stream) {
+    SB_ARG(W && x && y && K > 0 && N >= 0, "bad GEMV arguments");
+    SB_ARG(K % 8 == 0 && ALIGNED16(W) && ALIGNED16(x), "gemv_h needs K % 8 == 0 and 16-byte aligned W, x");
+    SB_ARG((size_t)K * 4 <= 200 * 1024, "gemv_h: K too large for the shared x stage");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr w = DP(W), xx = DP(x), b = DP(bias), yy = DP(y);
+    void *args[] = {&w, &xx, &b, &yy, &K, &N};
+    return sb_launch(c, F_GEMV_H_B200, gemv_grid(c, CEIL_DIV(N, 4), 8), 1, 256, (unsigned)K * 4,
+                     (CUstream)stream, args, 0);
+}
+
+int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream) {
+    SB_ARG(W && X && Y && K > 0 && N >= 0 && B >= 1 && B <= 8, "bad gemv_hh arguments");
+    SB_ARG(K % 8 == 0 && ALIGNED16(W) && ALIGNED16(X), "gemv_hh needs K % 8 == 0 and 16-byte aligned W, X");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    for (int b0 = 0; b0 < B;) {
+        int nb = B - b0 >= 4 ? 4 : (B - b0 >= 2 ? 2 : 1);
+        SB_ARG((size_t)nb * K * 4 <= 220 * 1024, "gemv_hh: batch x K too large for the shared x stage");
+        sb_fn_id f = nb == 4 ? F_GEMV_HH4 : (nb == 2 ? F_GEMV_HH2 : F_GEMV_HH1);
+        CUdeviceptr w = DP(W), xx = DP(X + (size_t)b0 * K), yy = DP(Y + (size_t)b0 * N);
+        void *args[] = {&w, &xx, &yy, &K, &N};
+        int rc = sb_launch(c, f, gemv_grid(c, CEIL_DIV(N, 4), 8), 1, 256, (unsigned)(nb * K * 4), (CUstream)stream,
+                           args, 0);
+        if (rc) return rc;
+        b0 += nb;
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------ elementwise / norms */
+int sb_rmsnorm(const float *x, const uint16_t *w, float *y, int n, float eps, int rows, void *stream) {
+    SB_ARG(x && w && y && n > 0 && rows >= 0, "bad rmsnorm arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr a = DP(x), b = DP(w), d = DP(y);
+    void *args[] = {&a, &b, &d, &n, &eps};
+    return sb_launch(c, F_RMSNORM, (unsigned)rows, 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+int sb_layernorm(const float *x, const float *w, const float *b, float *y, int n, float eps, int rows,
+                 void *stream) {
+    SB_ARG(x && w && b && y && n > 0 && rows >= 0, "bad layernorm arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr a = DP(x), ww = DP(w), bb = DP(b), d = DP(y);
+    void *args[] = {&a, &ww, &bb, &d, &n, &eps};
+    return sb_launch(c, F_LAYERNORM, (unsigned)rows, 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+int sb_rope(float *x, const float *cosT, const float *sinT, int T, int H, int HD, int pos0, void *stream) {
+    SB_ARG(x && cosT && sinT && T >= 0 && H > 0 && HD > 0 && HD % 2 == 0 && pos0 >= 0, "bad rope arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr a = DP(x), cc = DP(cosT), s = DP(sinT);
+    void *args[] = {&a, &cc, &s, &T, &H, &HD, &pos0};
+    long total = (long)T * H * (HD / 2);
+    return sb_launch(c, F_ROPE, (unsigned)(total ? CEIL_DIV(total, 256) : 0), 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+int sb_swiglu(const float *g, const float *u, float *y, int n, void *stream) {
+    SB_ARG(g && u && y && n >= 0, "bad swiglu arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr a = DP(g), b = DP(u), d = DP(y);
+    void *args[] = {&a, &b, &d, &n};
+    return sb_launch(c, F_SWIGLU, (unsigned)CEIL_DIV(n, 256), 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+int sb_gelu(const float *x, float *y, int n, void *stream) {
+    SB_ARG(x && y && n >= 0, "bad gelu arguments");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr a = DP(x), d = DP(y);
+    void *args[] = {&a, &d, &n};
+    return sb_launch(c, F_GELU, (unsigned)CEIL_DIV(n, 256), 1, 256, 0, (CUstream)stream, args, 0);
+}
+
+/* ------------------------------------------------------------------ attention */
+int sb_attn_decode(const float *q, const float *kc, const float *vc, float *out, int T, int NH, int NKV, int HD,
+                   int kv_stride, float scale, float *part, unsigned *counters, void *stream) {
+    SB_ARG(q && kc && vc && out && part && counters, "null pointer");
+    SB_ARG(T >= 1 && HD == 64 && NKV > 0 && NH % NKV == 0 && kv_stride >= NKV * HD && kv_stride % 2 == 0,
+           "attention: need T >= 1, HD == 64, NH % NKV == 0");
+    const int G = NH / NKV;
+    SB_ARG(G == 1 || G == 7, "attention: NH/NKV must be 1 (MHA) or 7 (Qwen GQA)");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    int max_splits = CEIL_DIV(T, 16);
+    CUdeviceptr a = DP(q), k = DP(kc), v = DP(vc), o = DP(out), p = DP(part), cn = DP(counters);
+    void *args[] = {&a, &k, &v, &T, &o, &p, &cn, &kv_stride, &scale, &max_splits};
+    return sb_launch(c, G == 7 ? F_ATTN_G7 : F_ATTN_G1, (unsigned)NKV, (unsigned)max_splits, 128, 0,
+                     (CUstream)stream, args, 0);
+}
