@@ -152,10 +152,20 @@ double sb_engine_step_bytes(sb_engine *e);
 /* Time `reps` standalone launches (CUDA events on the engine stream) of one
  * kernel of the step -- 1 QKV, 2 attention, 3 O-proj, 4 MLP up (gate|up or
  * fc), 5 MLP down, 6 LM head (layer 0 where it applies) -- each after an
- * optional memset of `flush` (an L2-sized device buffer) so weights come
- * from HBM.  Reports the average ms and the kernel's algorithmic bytes. */
+ * optional streaming read of `flush` (a device buffer larger than L2; at
+ * most 4*SMs*256 floats of the engine's logits buffer receive its sums) so
+ * the weights come from HBM.  Reports the average ms and the kernel's algorithmic bytes. */
 int sb_engine_profile(sb_engine *e, int which, int reps, void *flush, size_t flush_bytes, float *avg_ms,
                       double *bytes);
+
+/* ---- token selection -------------------------------------------------------
+ * Sampled next token with the reference Qwen engine's settings and step
+ * order (qwen_engine.c:366-404; it passes temperature 0.7, top_k 20,
+ * top_p 0.8, repetition penalty 1.1, xorshift state seeded 1234).  Given
+ * the same logits, context and state it draws the same token.  top_k <= 64;
+ * scratch (V floats) may be NULL.  Returns the id, or -1 on bad arguments. */
+int sb_sample_token(const float *logits, int V, const int *ctx, int ctx_len, float temperature, int top_k,
+                    float top_p, float rep_penalty, uint32_t *rng_state, float *scratch);
 
 /* ---- synthetic inputs in the reference layouts -----------------------------
  * Deterministic from `seed`: weights N(0, 0.02) (fp16 round-to-nearest for

@@ -97,11 +97,14 @@ def gemv_h(W16, x, bias=None):
 
 
 def h2f(bits):
-    """Vectorised reference fp16 decode (exponent 0 -> 0) of uint16 bits."""
-    bits = np.asarray(bits, dtype=np.uint16)
-    f = bits.view(np.float16).astype(np.float32)
-    f[(bits & 0x7C00) == 0] = 0.0
-    return f
+    """Vectorised reference fp16 decode of uint16 bits (qwen_engine.c:90-98):
+    exponent 0 -> 0, and no inf/NaN case (exponent 31 decodes to a finite
+    value, as in the reference)."""
+    h = np.asarray(bits, dtype=np.uint16).astype(np.uint32)
+    e = (h >> 10) & 0x1F
+    u = ((h & 0x8000) << 16) | ((e + 112) << 23) | ((h & 0x3FF) << 13)
+    u[e == 0] = 0
+    return u.astype(np.uint32).view(np.float32)
 
 
 def rmsnorm(x, w16, eps):

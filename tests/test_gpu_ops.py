@@ -78,7 +78,7 @@ def test_swiglu_gelu(cuda_dev):
     z = torch.zeros(3072, device="cuda")
     sb200.gelu(_t(x), z, 3072)
     torch.cuda.synchronize()
-    np.testing.assert_allclose(z.cpu().numpy(), orc.gelu(x), rtol=2e-6, atol=1e-7)
+    np.testing.assert_allclose(z.cpu().numpy(), orc.gelu(x), rtol=2e-6, atol=1e-6)  # tanhf ulps near 0
 
 
 @pytest.mark.parametrize("T", [1, 2, 15, 16, 17, 33, 288, 1000, 2048])
