@@ -104,6 +104,16 @@ int sb_swiglu(const float *g, const float *u, float *y, int n, void *stream);
  * attn_mix (gpt2_kernels.cu:221-268). */
 int sb_attn_decode(const float *q, const float *kc, const float *vc, float *out, int T, int NH, int NKV,
                    int HD, int kv_stride, float scale, float *part, unsigned *counters, void *stream);
+/* The same decode attention for callers that cannot allocate device memory
+ * (a fixed device budget sized at start-up, a host framework that owns every
+ * allocation, an allocation-free token loop): the partials and tickets live
+ * in a static array compiled into this library, at most T <= 2048 positions
+ * and NH <= 16 heads (larger requests return SB_ERR_ARG).  The first call on
+ * a device resolves that array's address (make it before any stream capture
+ * begins); all calls share the array, so calls that overlap on the GPU race.
+ * No counterpart in the reference, which has no scratch-using kernel. */
+int sb_attn_decode_noalloc(const float *q, const float *kc, const float *vc, float *out, int T, int NH, int NKV,
+                           int HD, int kv_stride, float scale, void *stream);
 int sb_layernorm(const float *x, const float *w, const float *b, float *y, int n, float eps, int rows,
                  void *stream);
 int sb_gelu(const float *x, float *y, int n, void *stream);

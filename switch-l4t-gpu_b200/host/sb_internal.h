@@ -7,6 +7,10 @@
 
 #include "../../include/switch_b200.h"
 
+#ifdef __cplusplus
+extern "C" {
+#endif
+
 enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_COUNT };
 
 typedef enum {
@@ -72,4 +76,7 @@ sb_ctx *sb_ctx_get(void);
 int sb_launch(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned bx, unsigned smem, CUstream s,
               void **args, int pdl);
 
+#ifdef __cplusplus
+}
+#endif
 #endif

@@ -84,6 +84,7 @@ def lib():
     _sig(L.sb_rope, I, P, P, P, I, I, I, I, P)
     _sig(L.sb_swiglu, I, P, P, P, I, P)
     _sig(L.sb_attn_decode, I, P, P, P, P, I, I, I, I, I, F, P, P, P)
+    _sig(L.sb_attn_decode_noalloc, I, P, P, P, P, I, I, I, I, I, F, P)
     _sig(L.sb_layernorm, I, P, P, P, P, I, F, I, P)
     _sig(L.sb_gelu, I, P, P, I, P)
     _sig(L.sb_engine_create, P, I, ctypes.c_char_p, I, ctypes.c_uint)
@@ -199,6 +200,11 @@ def swiglu(g, u, y, n, stream=None):
 def attn_decode(q, kc, vc, out, T, NH, NKV, HD, kv_stride, scale, part, counters, stream=None):
     check(lib().sb_attn_decode(_p(q), _p(kc), _p(vc), _p(out), T, NH, NKV, HD, kv_stride, scale,
                                _p(part), _p(counters), _s(stream)))
+
+
+def attn_decode_noalloc(q, kc, vc, out, T, NH, NKV, HD, kv_stride, scale, stream=None):
+    """sb_attn_decode without caller scratch (static device array, T <= 2048)."""
+    check(lib().sb_attn_decode_noalloc(_p(q), _p(kc), _p(vc), _p(out), T, NH, NKV, HD, kv_stride, scale, _s(stream)))
 
 
 def layernorm(x, w, b, y, n, eps, rows=1, stream=None):
