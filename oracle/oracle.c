@@ -113,13 +113,13 @@ double orc_freivalds(const float *A, const float *B, const float *C, int M, int 
     parallel_rows(mv_rows, &c2, M, nthreads);
     mv_ctx c3 = {C, r, cr, N};
     parallel_rows(mv_rows, &c3, M, nthreads);
-    double worst = 0;
+    double num = 0, den = 0;
     for (int i = 0; i < M; i++) {
-        double d = fabs(cr[i] - abr[i]) / fmax(1.0, fabs(abr[i]));
-        if (d > worst) worst = d;
+        num += (cr[i] - abr[i]) * (cr[i] - abr[i]);
+        den += abr[i] * abr[i];
     }
     free(r); free(br); free(abr); free(cr);
-    return worst;
+    return sqrt(num) / fmax(sqrt(den), 1e-300);
 }
 
 /* ------------------------------------------------------------------ GEMV */

@@ -38,8 +38,9 @@ void orc_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int 
 /* Harness tolerance check of gpu_workload.c:99-101: |d| > 0.05|ref| + 1e-3. */
 int orc_sgemm_bad_cells(const float *got, const float *ref, size_t n);
 
-/* Freivalds in double: returns max_i |(C r)_i - (A (B r))_i| / max(1,|(A(B r))_i|)
- * for a +-1 vector r from `seed`. */
+/* Freivalds in double: returns ||C r - A (B r)||_2 / ||A (B r)||_2 for a
+ * +-1 vector r from `seed` (about 1e-6 for a correct FP32 product; O(1) for
+ * a wrong tile). */
 double orc_freivalds(const float *A, const float *B, const float *C, int M, int N, int K,
                      uint64_t seed, int nthreads);
 
