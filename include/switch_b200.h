@@ -129,6 +129,8 @@ typedef struct sb_engine sb_engine;
 #define SB_MODEL_GPT2 2
 #define SB_FLAG_NO_GRAPH 1u  /* launch kernels directly instead of graph replay */
 #define SB_FLAG_NO_PDL 2u    /* no programmatic dependent launch            */
+#define SB_FLAG_MULTI_KERNEL 4u /* Qwen: one kernel per stage instead of the
+                                 * persistent whole-step kernel              */
 #define SB_GEN_STOP_EOS 1u   /* stop at the model's end tokens (reference behaviour) */
 
 /* max_ctx: KV-cache positions (<= 8192 Qwen, <= 1024 GPT-2). NULL on error. */
@@ -157,6 +159,15 @@ void *sb_engine_stream(sb_engine *e);
 int sb_engine_logits(sb_engine *e, const float **dev_logits, int *vocab);
 /* Kernel launches issued per decode step (with / without LM head). */
 int sb_engine_launches_per_step(sb_engine *e, int with_logits);
+/* 1 when the step runs as the persistent whole-step kernel (Qwen on GPUs
+ * with >= 128 SMs: one cooperative launch per token, grid-wide barriers
+ * between stages), 0 for one kernel per stage. */
+int sb_engine_uses_persistent_kernel(sb_engine *e);
+/* Profiling aid for the persistent kernel: dev_buf (u64[SMs][128][2], or
+ * NULL to stop) receives %globaltimer stamps at every grid barrier, per
+ * CTA: [cta][k][0] = arrival at barrier k, [cta][k][1] = release
+ * ([cta][0][0] = kernel start).  Graphs are re-captured on next use. */
+int sb_engine_set_trace(sb_engine *e, void *dev_buf);
 /* Bytes of weights a decode step streams (with LM head). */
 double sb_engine_step_bytes(sb_engine *e);
 /* Time `reps` standalone launches (CUDA events on the engine stream) of one

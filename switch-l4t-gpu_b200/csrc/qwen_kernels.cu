@@ -415,3 +415,8 @@ extern "C" __global__ void qwen_lmhead(const unsigned short *__restrict__ Wemb,
     if (threadIdx.x == 0 && best_s) atomicMax(&st->key, best_s);
 }
 
+
+// =====================================================================
+// Part 3 -- the persistent whole-step kernel
+// =====================================================================
+#include "qwen_mk.cuh"

@@ -23,6 +23,7 @@
 #include <string.h>
 #include <sys/stat.h>
 
+#include "../csrc/sb_mk_params.h"
 #include "../csrc/sb_step.h"
 #include "sb_internal.h"
 #include "sb_models.h"
@@ -44,7 +45,20 @@ struct sb_engine {
     int V, NL, kvw;
     CUgraphExec gexec[2];
     int n_prompt, n_end;
+    /* persistent whole-step kernel (Qwen) */
+    int mk;
+    CUdeviceptr bar, err;
+    int mk_splits, mk_score_cap;
+    unsigned mk_smem;
+    CUdeviceptr trace;
 };
+
+#define MK_THREADS 512
+#define MK_WARPS 16
+static unsigned mk_smem_bytes(int score_cap) {
+    /* x planes (FC floats) | 16 warp regions of 6x896 fp16 | scores | red(32) opart(8x64) ksum(16) */
+    return (unsigned)(QW_FC * 4 + MK_WARPS * 6 * QW_C * 2 + score_cap * 4 + (32 + 8 * 64 + 16) * 4);
+}
 
 /* ------------------------------------------------------------------ upload */
 static int upload_file(sb_engine *e, const char *path, size_t want) {
@@ -202,7 +216,32 @@ static int launch_kernel(sb_engine *e, int l, int which, int with_logits, int pd
                                      : launch_gpt2(e, l, which, with_logits, pdl);
 }
 
+static int record_mk(sb_engine *e, int with_logits) {
+    SB_CK(cuMemsetD32Async(e->bar, 0, 1, e->stream));
+    SbMkParams prm;
+    memset(&prm, 0, sizeof prm);
+    prm.w = e->w;
+    prm.kv = e->kv;
+    prm.x = e->x;
+    prm.q = e->q;
+    prm.part = e->part;
+    prm.hid = e->hid;
+    prm.logits = e->logits;
+    prm.st = e->step;
+    prm.tokens = e->tokens;
+    prm.bar = e->bar;
+    prm.err = e->err;
+    prm.trace = e->trace;
+    prm.ctx_cap = e->ctx_cap;
+    prm.with_logits = with_logits;
+    prm.splits = e->mk_splits;
+    prm.score_cap = e->mk_score_cap;
+    void *args[] = {&prm};
+    return sb_launch_coop(e->c, F_QWEN_MK, (unsigned)e->c->sms, MK_THREADS, e->mk_smem, e->stream, args);
+}
+
 static int record_model(sb_engine *e, int with_logits) {
+    if (e->mk) return record_mk(e, with_logits);
     const int pdl = pdl_on(e);
     int rc = launch_kernel(e, 0, SBK_EMBED, with_logits, pdl);
     for (int l = 0; !rc && l < e->NL; l++)
@@ -264,6 +303,16 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     e->kvw = qw ? QW_KVD : G2_C;
     e->wbytes = qw ? QW_FILE_BYTES : (size_t)G2_TOTAL_FLOATS * 4;
     e->max_splits = CEIL_DIV(max_ctx, 16);
+    /* the persistent kernel needs >= 128 co-resident CTAs (its per-CTA row
+     * shares are sized for that) and cooperative launch */
+    if (model == SB_MODEL_QWEN && !(flags & SB_FLAG_MULTI_KERNEL) && c->sms >= 128) {
+        e->mk_splits = c->sms / QW_NH;
+        e->mk_score_cap = CEIL_DIV(max_ctx, e->mk_splits) + 8;
+        e->mk_smem = mk_smem_bytes(e->mk_score_cap);
+        int coop = 0;
+        cuDeviceGetAttribute(&coop, CU_DEVICE_ATTRIBUTE_COOPERATIVE_LAUNCH, c->dev);
+        e->mk = coop && sb_occupancy(c, F_QWEN_MK, MK_THREADS, e->mk_smem) >= 1;
+    }
     const int groups = qw ? QW_NKV : G2_NH, G = qw ? QW_NH / QW_NKV : 1;
     const int C = qw ? QW_C : G2_C, FC = qw ? QW_FC : G2_FC, NQ = qw ? QW_C : G2_C;
 
@@ -280,15 +329,23 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     CARVE(att, NQ * 4);
     CARVE(hid, FC * 4);
     CARVE(logits, (size_t)e->V * 4);
-    CARVE(part, (size_t)groups * e->max_splits * G * 66 * 4);
+    {
+        size_t pf = (size_t)groups * e->max_splits * G * 66;
+        size_t pm = (size_t)QW_NH * (e->mk_splits > 0 ? e->mk_splits : 1) * 66;
+        CARVE(part, (pf > pm ? pf : pm) * 4);
+    }
     CARVE(counters, groups * 4);
     CARVE(step, sizeof(SbStep));
     CARVE(tokens, (size_t)(max_ctx + 2) * 4);
+    CARVE(bar, 4);
+    CARVE(err, 4);
 #undef CARVE
     if (cuMemAlloc(&e->scratch, off)) { sb_fail(SB_ERR_STATE, "scratch allocation", __FILE__, __LINE__); goto fail; }
     e->x += e->scratch; e->q += e->scratch; e->att += e->scratch; e->hid += e->scratch;
     e->logits += e->scratch; e->part += e->scratch; e->counters += e->scratch; e->step += e->scratch;
     e->tokens += e->scratch;
+    e->bar += e->scratch;
+    e->err += e->scratch;
     if (cuMemsetD8Async(e->scratch, 0, off, e->stream) || cuMemsetD8Async(e->kv, 0, kv_bytes, e->stream) ||
         cuStreamSynchronize(e->stream)) {
         sb_fail(SB_ERR_STATE, "initialisation", __FILE__, __LINE__);
@@ -330,6 +387,7 @@ int sb_engine_logits(sb_engine *e, const float **dev_logits, int *vocab) {
 
 int sb_engine_launches_per_step(sb_engine *e, int with_logits) {
     if (!e) return 0;
+    if (e->mk) return 1;
     return 1 + 5 * e->NL + (with_logits ? 1 : 0) + 1;
 }
 
@@ -345,6 +403,21 @@ double sb_engine_step_bytes(sb_engine *e) {
 }
 
 /* ------------------------------------------------------------------ stepping */
+/* A persistent-kernel barrier that timed out leaves *err set (the kernel
+ * returned early instead of hanging); report it and clear the flag. */
+static int check_device_error(sb_engine *e) {
+    if (!e->mk) return 0;
+    int err = 0;
+    SB_CK(cuMemcpyDtoHAsync(&err, e->err, 4, e->stream));
+    SB_CK(cuStreamSynchronize(e->stream));
+    if (err) {
+        SB_CK(cuMemsetD32Async(e->err, 0, 1, e->stream));
+        SB_CK(cuStreamSynchronize(e->stream));
+        return sb_fail(SB_ERR_STATE, "decode step aborted: a grid barrier wait timed out", __FILE__, __LINE__);
+    }
+    return 0;
+}
+
 static int put_step(sb_engine *e, const SbStep *st) {
     SB_CK(cuMemcpyHtoDAsync(e->step, st, sizeof *st, e->stream));
     return 0;
@@ -367,7 +440,7 @@ int sb_engine_forward(sb_engine *e, int token, int pos, int want_logits, float *
     if ((rc = run_step(e, want_logits ? 1 : 0))) return rc;
     if (want_logits && logits_host) SB_CK(cuMemcpyDtoHAsync(logits_host, e->logits, (size_t)e->V * 4, e->stream));
     SB_CK(cuStreamSynchronize(e->stream));
-    return 0;
+    return check_device_error(e);
 }
 
 int sb_engine_begin(sb_engine *e, const int *prompt, int n_prompt, int n_gen, unsigned gen_flags) {
@@ -408,6 +481,8 @@ int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out) {
     SbStep st;
     SB_CK(cuMemcpyDtoHAsync(&st, e->step, sizeof st, e->stream));
     SB_CK(cuStreamSynchronize(e->stream));
+    int rc = check_device_error(e);
+    if (rc) return rc;
     int n = e->n_prompt + st.n_generated;
     if (n > e->n_end) n = e->n_end;
     if (out_ids) {
@@ -484,5 +559,18 @@ int sb_engine_profile(sb_engine *e, int which, int reps, void *flush, size_t flu
     if (rc) return sb_fail(rc, "profile launch", __FILE__, __LINE__);
     if (avg_ms) *avg_ms = (float)(total / reps);
     if (bytes) *bytes = kernel_bytes(e, which);
+    return 0;
+}
+
+int sb_engine_uses_persistent_kernel(sb_engine *e) { return e && e->mk; }
+
+int sb_engine_set_trace(sb_engine *e, void *dev_buf) {
+    if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);
+    e->trace = (CUdeviceptr)(uintptr_t)dev_buf;
+    for (int i = 0; i < 2; i++)
+        if (e->gexec[i]) {
+            cuGraphExecDestroy(e->gexec[i]);
+            e->gexec[i] = NULL;
+        }
     return 0;
 }

@@ -45,6 +45,7 @@ typedef enum {
     F_QWEN_GATEUP,
     F_QWEN_LMHEAD,
     F_QWEN_FINALIZE,
+    F_QWEN_MK,
     F_COUNT
 } sb_fn_id;
 
@@ -75,6 +76,10 @@ sb_ctx *sb_ctx_get(void);
  * programmatic stream-serialisation attribute */
 int sb_launch(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned bx, unsigned smem, CUstream s,
               void **args, int pdl);
+/* cooperative launch (all CTAs co-resident, required by grid-wide barriers) */
+int sb_launch_coop(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned bx, unsigned smem, CUstream s, void **args);
+/* max co-resident CTAs of f per SM at this block size / dynamic smem */
+int sb_occupancy(sb_ctx *c, sb_fn_id f, int block, size_t smem);
 
 #ifdef __cplusplus
 }

@@ -62,6 +62,7 @@ static const struct {
     [F_QWEN_GATEUP] = {M_QWEN, "qwen_gateup_swiglu"},
     [F_QWEN_LMHEAD] = {M_QWEN, "qwen_lmhead"},
     [F_QWEN_FINALIZE] = {M_QWEN, "sb_finalize"},
+    [F_QWEN_MK] = {M_QWEN, "qwen_decode_mk"},
 };
 
 /* ---------------------------------------------------------------- errors */
@@ -168,6 +169,45 @@ int sb_launch(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned bx, unsi
     memset(&cfg, 0, sizeof cfg);
     cfg.gridDimX = gx;
     cfg.gridDimY = gy;
+    cfg.gridDimZ = 1;
+    cfg.blockDimX = bx;
+    cfg.blockDimY = 1;
+    cfg.blockDimZ = 1;
+    cfg.sharedMemBytes = smem;
+    cfg.hStream = s;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    SB_CK(cuLaunchKernelEx(&cfg, c->fn[f], args, NULL));
+    return 0;
+}
+
+static int resolve(sb_ctx *c, sb_fn_id f, unsigned smem) {
+    if (!c->fn[f]) SB_CK(cuModuleGetFunction(&c->fn[f], c->mod[fn_table[f].mod], fn_table[f].name));
+    if (smem > 48 * 1024 && c->smem_set[f] < (int)smem) {
+        SB_CK(cuFuncSetAttribute(c->fn[f], CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem));
+        c->smem_set[f] = (int)smem;
+    }
+    return 0;
+}
+
+int sb_occupancy(sb_ctx *c, sb_fn_id f, int block, size_t smem) {
+    int n = 0;
+    if (resolve(c, f, (unsigned)smem)) return 0;
+    if (cuOccupancyMaxActiveBlocksPerMultiprocessor(&n, c->fn[f], block, smem) != CUDA_SUCCESS) return 0;
+    return n;
+}
+
+int sb_launch_coop(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned bx, unsigned smem, CUstream s, void **args) {
+    int rc = resolve(c, f, smem);
+    if (rc) return rc;
+    CUlaunchAttribute attr;
+    memset(&attr, 0, sizeof attr);
+    attr.id = CU_LAUNCH_ATTRIBUTE_COOPERATIVE;
+    attr.value.cooperative = 1;
+    CUlaunchConfig cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.gridDimX = gx;
+    cfg.gridDimY = 1;
     cfg.gridDimZ = 1;
     cfg.blockDimX = bx;
     cfg.blockDimY = 1;

@@ -23,6 +23,7 @@ MODEL_QWEN = 1
 MODEL_GPT2 = 2
 FLAG_NO_GRAPH = 1
 FLAG_NO_PDL = 2
+FLAG_MULTI_KERNEL = 4
 GEN_STOP_EOS = 1
 
 QWEN = dict(V=151936, C=896, NL=24, NH=14, NKV=2, HD=64, FC=4864, CTX_FILE=8192,
@@ -99,6 +100,8 @@ def lib():
     _sig(L.sb_engine_logits, I, P, ctypes.POINTER(P), ctypes.POINTER(I))
     _sig(L.sb_engine_launches_per_step, I, P, I)
     _sig(L.sb_engine_step_bytes, D, P)
+    _sig(L.sb_engine_uses_persistent_kernel, I, P)
+    _sig(L.sb_engine_set_trace, I, P, P)
     _sig(L.sb_engine_profile, I, P, I, I, P, ctypes.c_size_t, ctypes.POINTER(F), ctypes.POINTER(D))
     _sig(L.sb_synth_weights, ctypes.c_long, I, ctypes.c_char_p, U64)
     _sig(L.sb_synth_ids, None, P, I, I, U64)
@@ -303,6 +306,13 @@ class Engine:
     @property
     def stream(self):
         return lib().sb_engine_stream(self.h)
+
+    def set_trace(self, buf):
+        check(lib().sb_engine_set_trace(self.h, _p(buf)))
+
+    @property
+    def persistent(self):
+        return bool(lib().sb_engine_uses_persistent_kernel(self.h))
 
     def launches_per_step(self, with_logits=True):
         return lib().sb_engine_launches_per_step(self.h, 1 if with_logits else 0)

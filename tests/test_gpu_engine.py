@@ -35,9 +35,20 @@ def _teacher_forced(model_id, weights, vocab, ctx, ids, flags=0):
         ref.close()
 
 
-def test_qwen_teacher_forced(cuda_dev, qwen_weights):
+@pytest.mark.parametrize("flags", [0, sb200.FLAG_MULTI_KERNEL])
+def test_qwen_teacher_forced(cuda_dev, qwen_weights, flags):
+    """flags 0: the persistent whole-step kernel; MULTI_KERNEL: one kernel per stage."""
     ids = sb200.synth_ids(12, sb200.QWEN["V"], 7)
-    _teacher_forced(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 64, ids)
+    _teacher_forced(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 64, ids, flags)
+
+
+def test_qwen_default_is_persistent(cuda_dev, qwen_weights):
+    eng = sb200.Engine(sb200.MODEL_QWEN, qwen_weights, 64)
+    try:
+        assert eng.persistent == (sb200.sm_count() >= 128)
+        assert eng.launches_per_step() == (1 if eng.persistent else 123)
+    finally:
+        eng.close()
 
 
 def test_gpt2_teacher_forced(cuda_dev, gpt2_weights):
@@ -45,12 +56,15 @@ def test_gpt2_teacher_forced(cuda_dev, gpt2_weights):
     _teacher_forced(sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"], 64, ids)
 
 
-@pytest.mark.parametrize("flags", [sb200.FLAG_NO_GRAPH, sb200.FLAG_NO_PDL, sb200.FLAG_NO_GRAPH | sb200.FLAG_NO_PDL])
-def test_qwen_launch_modes_agree(cuda_dev, qwen_weights, flags):
+@pytest.mark.parametrize("base,flags", [(0, sb200.FLAG_NO_GRAPH),
+                                        (sb200.FLAG_MULTI_KERNEL, sb200.FLAG_MULTI_KERNEL | sb200.FLAG_NO_GRAPH),
+                                        (sb200.FLAG_MULTI_KERNEL, sb200.FLAG_MULTI_KERNEL | sb200.FLAG_NO_PDL),
+                                        (sb200.FLAG_MULTI_KERNEL, sb200.FLAG_MULTI_KERNEL | 3)])
+def test_qwen_launch_modes_agree(cuda_dev, qwen_weights, base, flags):
     """Direct launches / no PDL produce bit-identical logits to graph replay."""
     ids = sb200.synth_ids(5, sb200.QWEN["V"], 9)
     outs = []
-    for f in (0, flags):
+    for f in (base, flags):
         eng = sb200.Engine(sb200.MODEL_QWEN, qwen_weights, 32, f)
         got = np.zeros(sb200.QWEN["V"], dtype=np.float32)
         for p, t in enumerate(ids):
@@ -60,10 +74,10 @@ def test_qwen_launch_modes_agree(cuda_dev, qwen_weights, flags):
     assert np.array_equal(outs[0], outs[1])
 
 
-def _greedy(model_id, weights, vocab, n_prompt, n_gen, seed):
+def _greedy(model_id, weights, vocab, n_prompt, n_gen, seed, flags=0):
     prompt = sb200.synth_ids(n_prompt, vocab, seed)
     name = "qwen" if model_id == sb200.MODEL_QWEN else "gpt2"
-    eng = sb200.Engine(model_id, weights, n_prompt + n_gen + 8)
+    eng = sb200.Engine(model_id, weights, n_prompt + n_gen + 8, flags)
     ref = orc.Model(name, weights, n_prompt + n_gen + 8, vocab)
     try:
         got = eng.generate(prompt, n_gen)
@@ -77,9 +91,10 @@ def _greedy(model_id, weights, vocab, n_prompt, n_gen, seed):
         ref.close()
 
 
-def test_qwen_greedy_64(cuda_dev, qwen_weights):
+@pytest.mark.parametrize("flags", [0, sb200.FLAG_MULTI_KERNEL])
+def test_qwen_greedy_64(cuda_dev, qwen_weights, flags):
     """configs[2] shape: 32 seeded prompt tokens, greedy, 64 steps identical."""
-    _greedy(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 32, 63, 32)
+    _greedy(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 32, 63, 32, flags)
 
 
 def test_gpt2_greedy_64(cuda_dev, gpt2_weights):
