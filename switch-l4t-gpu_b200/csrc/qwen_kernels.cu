@@ -416,6 +416,21 @@ extern "C" __global__ void qwen_lmhead(const unsigned short *__restrict__ Wemb,
 }
 
 
+// Flush fp16 subnormals (exponent 0) to +0 in place, 16 bytes per thread
+// step.  The reference decodes exponent-0 weights as 0 (qwen_engine.c:90-98);
+// once the engine's device copy holds them as 0, its kernels can use the
+// plain hardware conversion and get exactly the reference's values.
+extern "C" __global__ void fp16_flush_subnormals(uint4 *__restrict__ p, long n16) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n16; i += (long)gridDim.x * blockDim.x) {
+        uint4 w = p[i];
+        w.x = ftz_half2_bits(w.x);
+        w.y = ftz_half2_bits(w.y);
+        w.z = ftz_half2_bits(w.z);
+        w.w = ftz_half2_bits(w.w);
+        p[i] = w;
+    }
+}
+
 // =====================================================================
 // Part 3 -- the persistent whole-step kernel
 // =====================================================================

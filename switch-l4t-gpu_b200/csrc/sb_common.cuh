@@ -29,6 +29,38 @@ SB_DEV float h2f_ftz(uint16_t h) {
     return ((h & 0x7C00u) == 0) ? 0.0f : __half2float(__ushort_as_half(h));
 }
 
+// ---------------------------------------------------------------- packed FP32
+// Blackwell's two-wide FP32 FMA (fma.rn.f32x2): halves the FMA instruction
+// count of the dot products; each lane is still an IEEE FP32 fused
+// multiply-add.
+SB_DEV unsigned long long f2_pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+SB_DEV float f2_sum(unsigned long long v) {
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+    return a + b;
+}
+SB_DEV unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// acc += 8 fp16 weights (no subnormal flush: the data is pre-flushed) x 8 floats.
+SB_DEV unsigned long long dot8_h_f2(const uint4 &w, const float4 &lo, const float4 &hi, unsigned long long acc) {
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+    const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&w.z));
+    const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&w.w));
+    acc = ffma2(f2_pack(f0.x, f0.y), f2_pack(lo.x, lo.y), acc);
+    acc = ffma2(f2_pack(f1.x, f1.y), f2_pack(lo.z, lo.w), acc);
+    acc = ffma2(f2_pack(f2.x, f2.y), f2_pack(hi.x, hi.y), acc);
+    acc = ffma2(f2_pack(f3.x, f3.y), f2_pack(hi.z, hi.w), acc);
+    return acc;
+}
+
 // ---------------------------------------------------------------- loads
 // Weights are read exactly once per decode step: no L1 allocation, and a
 // 256-byte L2 fetch granule so DRAM sees full bursts.

@@ -56,8 +56,9 @@ struct sb_engine {
 #define MK_THREADS 512
 #define MK_WARPS 16
 static unsigned mk_smem_bytes(int score_cap) {
-    /* x planes (FC floats) | 16 warp regions of 6x896 fp16 | scores | red(32) opart(8x64) ksum(16) */
-    return (unsigned)(QW_FC * 4 + MK_WARPS * 6 * QW_C * 2 + score_cap * 4 + (32 + 8 * 64 + 16) * 4);
+    /* x planes (FC floats) | 16 warp regions of (6 rows + 1/2 row) of 896 fp16 | scores |
+     * red(32) opart(16x64) ksum(16) */
+    return (unsigned)(QW_FC * 4 + MK_WARPS * (6 * QW_C * 2 + QW_C) + score_cap * 4 + (32 + MK_WARPS * 64 + MK_WARPS) * 4);
 }
 
 /* ------------------------------------------------------------------ upload */
@@ -307,7 +308,8 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
      * shares are sized for that) and cooperative launch */
     if (model == SB_MODEL_QWEN && !(flags & SB_FLAG_MULTI_KERNEL) && c->sms >= 128) {
         e->mk_splits = c->sms / QW_NH;
-        e->mk_score_cap = CEIL_DIV(max_ctx, e->mk_splits) + 8;
+        if (e->mk_splits > 16) e->mk_splits = 16; /* the combine handles <= 16 splits per head */
+        e->mk_score_cap = (CEIL_DIV(max_ctx, e->mk_splits) + 8 + 3) & ~3; /* multiple of 4 floats */
         e->mk_smem = mk_smem_bytes(e->mk_score_cap);
         int coop = 0;
         cuDeviceGetAttribute(&coop, CU_DEVICE_ATTRIBUTE_COOPERATIVE_LAUNCH, c->dev);
@@ -319,6 +321,18 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     if (cuStreamCreate(&e->stream, CU_STREAM_NON_BLOCKING)) { sb_fail(SB_ERR_STATE, "stream", __FILE__, __LINE__); goto fail; }
     if (cuMemAlloc(&e->w, e->wbytes)) { sb_fail(SB_ERR_STATE, "weight allocation", __FILE__, __LINE__); goto fail; }
     if (upload_file(e, weights_path, e->wbytes)) goto fail;
+    if (qw) {
+        /* fp16 regions (embedding; layers + final norm) -- not the fp32 RoPE
+         * tables between them: subnormals -> 0 once, as the reference decodes */
+        const size_t regions[2][2] = {{0, QW_OFF_COS}, {QW_LBASE, QW_FILE_BYTES}};
+        for (int k = 0; k < 2; k++) {
+            CUdeviceptr base = e->w + regions[k][0];
+            long n16 = (long)((regions[k][1] - regions[k][0]) / 16);
+            void *a[] = {&base, &n16};
+            if (sb_launch(c, F_FP16_FLUSH, 4 * c->sms, 1, 256, 0, e->stream, a, 0)) goto fail;
+        }
+        if (cuStreamSynchronize(e->stream)) { sb_fail(SB_ERR_STATE, "weight flush", __FILE__, __LINE__); goto fail; }
+    }
     const size_t kv_bytes = (size_t)2 * e->NL * max_ctx * e->kvw * 4;
     if (cuMemAlloc(&e->kv, kv_bytes)) { sb_fail(SB_ERR_STATE, "KV allocation", __FILE__, __LINE__); goto fail; }
     /* scratch: x[C] q[NQ] att[NQ] hid[FC] logits[V] part counters step tokens */

@@ -46,6 +46,7 @@ typedef enum {
     F_QWEN_LMHEAD,
     F_QWEN_FINALIZE,
     F_QWEN_MK,
+    F_FP16_FLUSH,
     F_COUNT
 } sb_fn_id;
 

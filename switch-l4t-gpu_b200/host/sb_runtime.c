@@ -63,6 +63,7 @@ static const struct {
     [F_QWEN_LMHEAD] = {M_QWEN, "qwen_lmhead"},
     [F_QWEN_FINALIZE] = {M_QWEN, "sb_finalize"},
     [F_QWEN_MK] = {M_QWEN, "qwen_decode_mk"},
+    [F_FP16_FLUSH] = {M_QWEN, "fp16_flush_subnormals"},
 };
 
 /* ---------------------------------------------------------------- errors */
