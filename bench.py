@@ -43,6 +43,7 @@ METRIC = "Qwen-0.5B-shape FP16 decode tok/s"
 UNIT = "tok/s"
 BASELINE_TOKS = 8.9  # Qwen2.5-0.5B FP16 decode on Tegra X1 (gpu-llm/STATUS.md:112)
 FALLBACK_HBM_GBS = 6650.0
+CPU_SAMPLE_TOKENS = 16  # per host core: about 10 s of reference CPU decode
 CONFIG = {
     "workload": "qwen2.5-0.5b-fp16-decode (configs[2])",
     "arch": "Qwen2.5-0.5B: 24 layers, hidden 896, 14q/2kv heads x 64, SwiGLU 4864, vocab 151936 tied",
@@ -185,10 +186,10 @@ def cpu_baseline(path):
     """Reference CPU decode on this host's cores, bounded sample (rank 0, N=1)."""
     cores = host_cores()
     if ref_bench_exe():
-        r = run_ref_bench(path, cores, 0, 1, 2)
+        r = run_ref_bench(path, cores, 0, 1, CPU_SAMPLE_TOKENS)
         return {"value": round(r["tok_s"], 4), "unit": UNIT, "cores": cores, "kind": "reference",
                 "sample": f"{cores} forked replicas of the reference cpu_forward (qwen_engine.c:292-358) + argmax, "
-                          f"2 greedy decode tokens each; {r['timed_s']:.1f} s wall"}
+                          f"{CPU_SAMPLE_TOKENS} greedy decode tokens each; {r['timed_s']:.1f} s wall"}
     # oracle restatement (row-parallel threads) when the reference build is absent
     sys.path.insert(0, os.path.join(REPO, "tests"))
     import numpy as np

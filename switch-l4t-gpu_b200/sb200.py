@@ -329,3 +329,14 @@ class Engine:
         by = ctypes.c_double()
         check(lib().sb_engine_profile(self.h, which, reps, _p(flush), flush_bytes, ctypes.byref(ms), ctypes.byref(by)))
         return ms.value, by.value
+
+
+if __name__ == "__main__":
+    # python sb200.py synth {qwen|gpt2} PATH SEED -- write a seeded synthetic
+    # weight file in the reference layout (used by profiling commands).
+    import sys
+    if len(sys.argv) == 5 and sys.argv[1] == "synth" and sys.argv[2] in ("qwen", "gpt2"):
+        model = MODEL_QWEN if sys.argv[2] == "qwen" else MODEL_GPT2
+        print(synth_weights(model, sys.argv[3], int(sys.argv[4])), "bytes written to", sys.argv[3])
+    else:
+        sys.exit("usage: sb200.py synth {qwen|gpt2} PATH SEED")
