@@ -20,6 +20,12 @@ N > 1 (torchrun): one independent replica per GPU (decode does not shard);
 scaling "weak".  The weights (988 MB) exceed the 126 MB L2, so no flush is
 needed between timed steps.
 
+Secondary keys of the same line: "sgemm" -- 16384^3 FP32 SGEMM sharded by
+row panels over all ranks (strong scaling) with the NCCL all-gather of C,
+compute-only and with the gather, per-GPU fraction of the live FP32 FMA
+peak; "gemv" -- the standalone FP16 GEMV sweep (batch 1 and 4) in GB/s
+against the HBM peak.
+
 `--impl reference` times the reference's own CPU decode (cpu_forward of
 gpu-llm/engine/qwen_engine.c compiled unmodified into oracle/_ref) on the
 host cores, one forked replica per core, on the same metric.
@@ -230,6 +236,111 @@ def run_reference_arm(args):
     print(json.dumps(line))
 
 
+# ------------------------------------------------------------------ secondary GPU measurements
+SGEMM_N = 16384
+GEMV_SHAPES = [(896, 896), (4864, 896), (896, 4864), (151936, 896), (32768, 8192)]
+
+
+def fp32_peak_tflops(torch, dev):
+    """Live FP32 FMA throughput of this GPU (fma_peak kernel, CUDA events)."""
+    import sb200
+    out = torch.empty(8 * sb200.sm_count() * 256, dtype=torch.float32, device=dev)  # grid 8 x SMs of 256
+    sb200.fma_peak(out, 2000)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    flops = sb200.fma_peak(out, 20000)
+    e1.record()
+    e1.synchronize()
+    return flops / (e0.elapsed_time(e1) * 1e-3) / 1e12
+
+
+def sgemm_section(torch, dev, dist_on, steps, warmup):
+    """16384^3 FP32 SGEMM row-panel sharded over all ranks (strong scaling):
+    compute-only and with the NCCL all-gather of C, max over ranks."""
+    import sgemm_dist
+    n = SGEMM_N
+    ps = sgemm_dist.PanelSgemm(n, n, n)
+    gA = torch.Generator(device=dev)
+    gA.manual_seed(5000 + RANK)
+    gB = torch.Generator(device=dev)
+    gB.manual_seed(777)  # B is the same on every rank
+    A = torch.rand(ps.rows, n, generator=gA, device=dev) * 2 - 1
+    B = torch.rand(n, n, generator=gB, device=dev) * 2 - 1
+    peak = fp32_peak_tflops(torch, dev)
+    cur = torch.cuda.current_stream(dev)
+
+    def step():
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(cur)
+        ps.multiply(A, B)
+        e1.record(cur)
+        if ps.world > 1:  # the gather PanelSgemm.__call__ issues after the product
+            torch.distributed.all_gather_into_tensor(ps.C_pad, ps.C_pad[ps.rank * ps.R:(ps.rank + 1) * ps.R])
+        e2.record(cur)
+        return e0, e1, e2
+
+    for _ in range(max(1, warmup)):
+        step()
+    torch.cuda.synchronize()
+    evs = [step() for _ in range(steps)]
+    torch.cuda.synchronize()
+    comp = sum(a.elapsed_time(b) for a, b, _ in evs)
+    tot = sum(a.elapsed_time(c) for a, _, c in evs)
+    t = torch.tensor([comp, tot], dtype=torch.float64, device=dev)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    comp_ms, tot_ms = float(t[0]) / steps, float(t[1]) / steps
+    flop = 2.0 * n ** 3
+    per_gpu = 2.0 * ps.rows * n * n / (comp_ms * 1e-3) / 1e12
+    res = {"metric": "SGEMM TFLOPS", "n": n, "value": round(flop / (tot_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "compute_tflops": round(flop / (comp_ms * 1e-3) / 1e12, 2), "ms_per_step": round(tot_ms, 3),
+           "compute_ms": round(comp_ms, 3), "allgather_ms": round(tot_ms - comp_ms, 3), "n_gpus": WORLD,
+           "scaling": "strong", "steps": steps,
+           "parallelism": f"row panels x{WORLD}, B replicated" + (", NCCL all-gather of C" if WORLD > 1 else ""),
+           "kernel": "sgemm_b200 (FP32 FFMA2, 128x128x8 tiles, 2 CTAs/SM)", "dtype": "f32",
+           "roofline": {"bound": "fp32", "achieved": round(per_gpu, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                        "frac": round(per_gpu / peak, 4), "peak_source": "fma_peak kernel, this run (of measured)"},
+           "l2": "no flush: 1 GiB operands > 126 MB L2"}
+    del A, B, ps
+    torch.cuda.empty_cache()
+    return res
+
+
+def gemv_section(torch, dev):
+    """Standalone FP16 GEMV sweep y = W.x (fp16 W and x, fp32 y) at batch 1
+    and 4; W copies rotated through 1 GiB so every launch streams from HBM."""
+    import sb200
+    peaks = measured_peaks()
+    peak = float(peaks["hbm_gbs"]) if peaks and peaks.get("hbm_gbs") else FALLBACK_HBM_GBS
+    pool = torch.empty(1 << 29, dtype=torch.float16, device=dev).normal_(0, 0.02)  # 1 GiB
+    out = {}
+    for (N, K) in GEMV_SHAPES:
+        wsz = N * K
+        ncopy = max(1, min(64, pool.numel() // wsz))
+        reps = max(8, min(400, int(4e9 / (wsz * 2))))
+        for Bw in (1, 4):
+            X = torch.randn(Bw, K, device=dev).half()
+            Y = torch.empty(Bw, N, device=dev)
+            for i in range(min(ncopy, 4)):
+                sb200.gemv_hh(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for r in range(reps):
+                i = r % ncopy
+                sb200.gemv_hh(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw)
+            e1.record()
+            e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            nbytes = wsz * 2 + Bw * K * 2 + Bw * N * 4
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out[f"{N}x{K}_b{Bw}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
+                                     "l2": "rotating copies" if ncopy * wsz * 2 > 4 * 126e6 else "L2-resident"}
+    del pool
+    torch.cuda.empty_cache()
+    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "gemv_hh1/gemv_hh4", "peak": peak, "unit": "GB/s",
+            "shapes": out}
+
+
 # ------------------------------------------------------------------ GPU arm
 def run_b200(args):
     import torch
@@ -370,6 +481,9 @@ def run_b200(args):
         "wall_s_timed": round(wall, 3),
     }
     eng.close()
+    if not args.no_secondary:
+        line["sgemm"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3)
+        line["gemv"] = gemv_section(torch, dev)
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_baseline(path)
@@ -390,6 +504,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the SGEMM and GEMV sweep measurements")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

@@ -43,6 +43,9 @@ SB_DEV float f2_sum(unsigned long long v) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
     return a + b;
 }
+SB_DEV void f2_unpack(unsigned long long v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
 SB_DEV unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
     unsigned long long d;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));

@@ -4,102 +4,88 @@
 // entry points.
 //
 // SGEMM design (FP32 CUDA cores; B200 has no FP32 tensor path):
-//   * 128x128 CTA tile, BK-deep k-slices, 256 threads, 8x8 outputs per
+//   * 128x128 CTA tile, 8-deep k-slices, 256 threads, 8x8 outputs per
 //     thread as 2x2 blocks of 4x4 (rows ty*4 and 64+ty*4, cols tx*4 and
 //     64+tx*4).  A warp covers 4 (ty) x 8 (tx) threads, so each 128-bit
 //     fragment load from shared memory touches 4 or 8 distinct 16-byte words:
 //     one wavefront, broadcast to the other lanes.
+//   * Packed FP32 FMA (fma.rn.f32x2): each instruction updates two adjacent
+//     columns of one output row, so the 64 FMAs of a k-step issue as 32
+//     instructions and the issue slots left over hide the fragment loads.
+//     Every output is still one fma.rn chain over k in order, so results are
+//     bit-identical to a scalar fmaf loop.
+//   * 128 registers per thread: two CTAs (16 warps) per SM, so one CTA's
+//     barrier and tile prologue overlap the other's FMAs.
 //   * A is stored k-major (transposed) in shared memory; its 16-byte units
-//     are XOR-swizzled by k (unit ^ 2*(k/4)) so the transposing 32-bit stores
-//     of a warp hit 32 distinct banks while fragment reads stay 128-bit.
-//     B is stored as loaded.  Two shared buffers: the next k-slice is fetched into
-//     registers while the current one is multiplied, then stored into the
-//     other buffer -- one __syncthreads per slice.
+//     are XOR-swizzled by k (unit ^ 4*(k/4)) so the transposing 32-bit stores
+//     of a warp (16 rows x 2 k-quads) hit 32 distinct banks while fragment
+//     reads stay 128-bit.  B is stored as loaded.  Two shared buffers: the
+//     next k-slice is fetched into registers while the current one is
+//     multiplied, then stored into the other buffer -- one __syncthreads per
+//     slice.
 //   * Tiles are walked by a grid-stride loop over a grouped (8 tile-rows)
 //     order, so ANY grid shape is correct -- the stock harness launches
 //     (n/32)^2 or (n/64)^2 CTAs of 16x16 threads (gpu_workload.c:90,142,168)
-//     and no dynamic shared memory (all 33 KB here are static).
-//   * Edges are predicated (zero-filled loads, guarded stores), so M, N, K
-//     need not be multiples of anything; 128-bit global loads are used when
-//     K and N are multiples of 4 and the pointers are 16-byte aligned.
+//     and no dynamic shared memory (the 16 KB here are static).  This
+//     package launches one CTA per tile.
+//   * Shapes that are multiples of the tile (M, N of 128, K of 8) with
+//     16-byte aligned pointers take unpredicated 128-bit loads and stores;
+//     anything else takes the same loop with zero-filled predicated scalar
+//     loads and guarded stores.
 #include "sb_common.cuh"
 
 #define SG_BM 128
 #define SG_BN 128
-#define SG_BK 16
+#define SG_BK 8
 #define SG_THREADS 256
 
 struct SgSmem {
     float As[2][SG_BK][SG_BM];  // k-major, 16-byte units swizzled by sg_swz(k)
     float Bs[2][SG_BK][SG_BN];
 };
-__device__ __forceinline__ int sg_swz(int k) { return (k >> 2) << 1; }
+__device__ __forceinline__ int sg_swz(int k) { return (k >> 2) << 2; }
 
-template <bool VEC>
+// One k-slice into registers with zero fill outside the matrices: A row
+// m0+ar, k-quad k0+ak; B k-row k0+br, columns n0+bc..+3.
 __device__ __forceinline__ void sg_load_slice(const float *__restrict__ A, const float *__restrict__ B, int M,
-                                              int N, int K, int m0, int n0, int k0, int tid, float4 (&ra)[2],
-                                              float4 (&rb)[2]) {
-    // A slice: 128 rows x 16 k = 512 float4; thread loads rows tid>>2 and
-    // 64+(tid>>2), k-quad (tid&3)*4.
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int r = m0 + h * 64 + (tid >> 2), c = k0 + (tid & 3) * 4;
-        if (VEC) {
-            ra[h] = (r < M && c < K) ? __ldg(reinterpret_cast<const float4 *>(A + (size_t)r * K + c))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-            const float *p = A + (size_t)r * K;
-            ra[h].x = (r < M && c + 0 < K) ? p[c + 0] : 0.f;
-            ra[h].y = (r < M && c + 1 < K) ? p[c + 1] : 0.f;
-            ra[h].z = (r < M && c + 2 < K) ? p[c + 2] : 0.f;
-            ra[h].w = (r < M && c + 3 < K) ? p[c + 3] : 0.f;
-        }
-    }
-    // B slice: 16 k-rows x 128 cols = 512 float4; thread loads k-rows
-    // tid>>5 and 8+(tid>>5), col quad (tid&31)*4.
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int r = k0 + h * 8 + (tid >> 5), c = n0 + (tid & 31) * 4;
-        if (VEC) {
-            rb[h] = (r < K && c < N) ? __ldg(reinterpret_cast<const float4 *>(B + (size_t)r * N + c))
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-            const float *p = B + (size_t)r * N;
-            rb[h].x = (r < K && c + 0 < N) ? p[c + 0] : 0.f;
-            rb[h].y = (r < K && c + 1 < N) ? p[c + 1] : 0.f;
-            rb[h].z = (r < K && c + 2 < N) ? p[c + 2] : 0.f;
-            rb[h].w = (r < K && c + 3 < N) ? p[c + 3] : 0.f;
-        }
-    }
+                                              int N, int K, int m0, int n0, int k0, int ar, int ak, int br, int bc,
+                                              float4 &ra, float4 &rb) {
+    const int r = m0 + ar, c = k0 + ak;
+    const float *pa = A + (size_t)r * K;
+    ra.x = (r < M && c + 0 < K) ? pa[c + 0] : 0.f;
+    ra.y = (r < M && c + 1 < K) ? pa[c + 1] : 0.f;
+    ra.z = (r < M && c + 2 < K) ? pa[c + 2] : 0.f;
+    ra.w = (r < M && c + 3 < K) ? pa[c + 3] : 0.f;
+    const int kr = k0 + br, n = n0 + bc;
+    const float *pb = B + (size_t)kr * N;
+    rb.x = (kr < K && n + 0 < N) ? pb[n + 0] : 0.f;
+    rb.y = (kr < K && n + 1 < N) ? pb[n + 1] : 0.f;
+    rb.z = (kr < K && n + 2 < N) ? pb[n + 2] : 0.f;
+    rb.w = (kr < K && n + 3 < N) ? pb[n + 3] : 0.f;
 }
 
-__device__ __forceinline__ void sg_store_slice(SgSmem &s, int buf, int tid, const float4 (&ra)[2],
-                                               const float4 (&rb)[2]) {
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int m = h * 64 + (tid >> 2), k = (tid & 3) * 4;
-        const int ms = (((m >> 2) ^ sg_swz(k)) << 2) | (m & 3);  // same swizzle for k..k+3
-        s.As[buf][k + 0][ms] = ra[h].x;
-        s.As[buf][k + 1][ms] = ra[h].y;
-        s.As[buf][k + 2][ms] = ra[h].z;
-        s.As[buf][k + 3][ms] = ra[h].w;
-    }
-#pragma unroll
-    for (int h = 0; h < 2; h++)
-        *reinterpret_cast<float4 *>(&s.Bs[buf][h * 8 + (tid >> 5)][(tid & 31) * 4]) = rb[h];
+__device__ __forceinline__ void sg_store_slice(SgSmem &s, int buf, int ams, int ak, int br, int bc, const float4 &ra,
+                                               const float4 &rb) {
+    s.As[buf][ak + 0][ams] = ra.x;
+    s.As[buf][ak + 1][ams] = ra.y;
+    s.As[buf][ak + 2][ams] = ra.z;
+    s.As[buf][ak + 3][ams] = ra.w;
+    *reinterpret_cast<float4 *>(&s.Bs[buf][br][bc]) = rb;
 }
 
-template <bool VEC>
+template <bool EDGE>
 __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const float *__restrict__ B,
                                             float *__restrict__ C, int M, int N, int K, int tid, int cta,
                                             int ncta, SgSmem &s) {
     const int warp = tid >> 5, lane = tid & 31;
     const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15
     const int tx = (warp & 1) * 8 + (lane & 7);    // 0..15
+    const int ar = tid >> 1, ak = (tid & 1) * 4;   // A loader: row, k-quad
+    const int br = tid >> 5, bc = (tid & 31) * 4;  // B loader: k-row, column quad
+    const int ams = (((ar >> 2) ^ sg_swz(ak)) << 2) | (ar & 3);
     const int tiles_m = (M + SG_BM - 1) / SG_BM, tiles_n = (N + SG_BN - 1) / SG_BN;
     const int ntiles = tiles_m * tiles_n;
     const int nk = (K + SG_BK - 1) / SG_BK;
-    const bool cvec = ((N & 3) == 0) && ((((uintptr_t)C) & 15) == 0);
 
     for (int tile = cta; tile < ntiles; tile += ncta) {
         // grouped raster: 8 tile-rows share the B column panels in L2
@@ -110,20 +96,37 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
         const int tn = (tile % per_group) / gsz;
         const int m0 = tm * SG_BM, n0 = tn * SG_BN;
 
-        float acc[8][8];
+        unsigned long long acc[8][4];  // (row i, column pair j) as packed f32x2
 #pragma unroll
         for (int i = 0; i < 8; i++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+            for (int j = 0; j < 4; j++) acc[i][j] = 0ull;
 
-        float4 ra[2], rb[2];
-        sg_load_slice<VEC>(A, B, M, N, K, m0, n0, 0, tid, ra, rb);
+        // unpredicated path: running pointers to this thread's A row / B k-row
+        const float *Ap = A + (size_t)(m0 + ar) * K + ak;
+        const float *Bp = B + (size_t)br * N + n0 + bc;
+        float4 ra, rb;
+        if (EDGE) {
+            sg_load_slice(A, B, M, N, K, m0, n0, 0, ar, ak, br, bc, ra, rb);
+        } else {
+            ra = __ldg(reinterpret_cast<const float4 *>(Ap));
+            rb = __ldg(reinterpret_cast<const float4 *>(Bp));
+        }
         __syncthreads();  // previous tile's readers are done with buffer 0
-        sg_store_slice(s, 0, tid, ra, rb);
+        sg_store_slice(s, 0, ams, ak, br, bc, ra, rb);
         __syncthreads();
         for (int kt = 0; kt < nk; kt++) {
             const int buf = kt & 1;
-            if (kt + 1 < nk) sg_load_slice<VEC>(A, B, M, N, K, m0, n0, (kt + 1) * SG_BK, tid, ra, rb);
+            if (kt + 1 < nk) {
+                if (EDGE) {
+                    sg_load_slice(A, B, M, N, K, m0, n0, (kt + 1) * SG_BK, ar, ak, br, bc, ra, rb);
+                } else {
+                    Ap += SG_BK;
+                    Bp += (size_t)SG_BK * N;
+                    ra = __ldg(reinterpret_cast<const float4 *>(Ap));
+                    rb = __ldg(reinterpret_cast<const float4 *>(Bp));
+                }
+            }
 #pragma unroll
             for (int k = 0; k < SG_BK; k++) {
                 const float4 a0 = *reinterpret_cast<const float4 *>(&s.As[buf][k][(ty ^ sg_swz(k)) * 4]);
@@ -131,31 +134,36 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
                 const float4 b0 = *reinterpret_cast<const float4 *>(&s.Bs[buf][k][tx * 4]);
                 const float4 b1 = *reinterpret_cast<const float4 *>(&s.Bs[buf][k][64 + tx * 4]);
                 const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                const unsigned long long bp[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y),
+                                                  f2_pack(b1.z, b1.w)};
 #pragma unroll
-                for (int i = 0; i < 8; i++)
+                for (int i = 0; i < 8; i++) {
+                    const unsigned long long ai = f2_pack(a[i], a[i]);
 #pragma unroll
-                    for (int j = 0; j < 8; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                    for (int j = 0; j < 4; j++) acc[i][j] = ffma2(ai, bp[j], acc[i][j]);
+                }
             }
-            if (kt + 1 < nk) sg_store_slice(s, buf ^ 1, tid, ra, rb);
+            if (kt + 1 < nk) sg_store_slice(s, buf ^ 1, ams, ak, br, bc, ra, rb);
             __syncthreads();
         }
         // epilogue
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int r = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
-            if (r >= M) continue;
 #pragma unroll
             for (int hb = 0; hb < 2; hb++) {
                 const int c = n0 + hb * 64 + tx * 4;
+                float4 o;
+                f2_unpack(acc[i][hb * 2], o.x, o.y);
+                f2_unpack(acc[i][hb * 2 + 1], o.z, o.w);
                 float *p = C + (size_t)r * N + c;
-                if (cvec && c + 3 < N) {
-                    *reinterpret_cast<float4 *>(p) =
-                        make_float4(acc[i][hb * 4 + 0], acc[i][hb * 4 + 1], acc[i][hb * 4 + 2], acc[i][hb * 4 + 3]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        if (c + j < N) p[j] = acc[i][hb * 4 + j];
+                if (!EDGE) {
+                    *reinterpret_cast<float4 *>(p) = o;
+                } else if (r < M) {
+                    if (c + 0 < N) p[0] = o.x;
+                    if (c + 1 < N) p[1] = o.y;
+                    if (c + 2 < N) p[2] = o.z;
+                    if (c + 3 < N) p[3] = o.w;
                 }
             }
         }
@@ -164,7 +172,7 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
 
 // Any-shape fallback for launches whose block is not 256 threads: each
 // thread computes whole outputs.
-__device__ void sgemm_any(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M,
+__device__ __noinline__ void sgemm_any(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M,
                           int N, int K) {
     const long nthreads = (long)gridDim.x * gridDim.y * gridDim.z * blockDim.x * blockDim.y * blockDim.z;
     const long cta = (blockIdx.z * gridDim.y + blockIdx.y) * (long)gridDim.x + blockIdx.x;
@@ -178,37 +186,44 @@ __device__ void sgemm_any(const float *__restrict__ A, const float *__restrict__
     }
 }
 
+// The predicated path as its own (not inlined) function, so its extra
+// registers do not constrain the allocation of the unpredicated loop.
+__device__ __noinline__ void sgemm_edge(const float *A, const float *B, float *C, int M, int N, int K, int tid,
+                                        int cta, int ncta, SgSmem &s) {
+    sgemm_tiles<true>(A, B, C, M, N, K, tid, cta, ncta, s);
+}
+
 __device__ __forceinline__ void sgemm_entry(const float *A, const float *B, float *C, int M, int N, int K) {
     const int nth = blockDim.x * blockDim.y * blockDim.z;
     if (nth != SG_THREADS) { sgemm_any(A, B, C, M, N, K); return; }
     const int tid = (threadIdx.z * blockDim.y + threadIdx.y) * blockDim.x + threadIdx.x;
     const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     const int ncta = gridDim.x * gridDim.y * gridDim.z;
-    const bool vec = ((K & 3) == 0) && ((N & 3) == 0) && ((((uintptr_t)A) & 15) == 0) &&
-                     ((((uintptr_t)B) & 15) == 0);
+    const bool whole = (M % SG_BM) == 0 && (N % SG_BN) == 0 && (K % SG_BK) == 0 &&
+                       ((((uintptr_t)A) | ((uintptr_t)B) | ((uintptr_t)C)) & 15) == 0;
     __shared__ __align__(16) SgSmem s;
-    if (vec) sgemm_tiles<true>(A, B, C, M, N, K, tid, cta, ncta, s);
-    else sgemm_tiles<false>(A, B, C, M, N, K, tid, cta, ncta, s);
+    if (whole) sgemm_tiles<false>(A, B, C, M, N, K, tid, cta, ncta, s);
+    else sgemm_edge(A, B, C, M, N, K, tid, cta, ncta, s);
 }
 
 // Reference: switch_gpu.cu:5-39 (stock launch: grid (n/32, n/32), block 16x16).
-extern "C" __global__ void __launch_bounds__(256, 1)
+extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_tiled(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
     sgemm_entry(A, B, C, M, N, K);
 }
 // Reference: switch_gpu.cu:59-95 (stock launch: grid (n/64, n/64), block 16x16).
-extern "C" __global__ void __launch_bounds__(256, 1)
+extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_tiled4(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
     sgemm_entry(A, B, C, M, N, K);
 }
 // Reference: switch_gpu.cu:99-137 (stock launch: grid (n/64, n/64), block 16x16).
-extern "C" __global__ void __launch_bounds__(256, 1)
+extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_opt(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
     sgemm_entry(A, B, C, M, N, K);
 }
-// This package's launch of the same kernel body: grid = min(tiles, 2*SMs),
+// This package's launch of the same kernel body: one CTA per 128x128 tile,
 // block 256 (issued by sb_sgemm).
-extern "C" __global__ void __launch_bounds__(256, 1)
+extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_b200(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
     sgemm_entry(A, B, C, M, N, K);
 }

@@ -162,7 +162,7 @@ int main(int argc, char **argv) {
             if (!k->f) continue;
             unsigned gx, gy = 1;
             if (k->tile) { gx = (unsigned)((n + k->tile - 1) / k->tile); gy = gx; }
-            else { long t = (long)((n + 127) / 128) * ((n + 127) / 128); gx = (unsigned)(t < sms ? t : sms); }
+            else gx = (unsigned)((n + 127) / 128) * (unsigned)((n + 127) / 128); /* one CTA per tile */
             const unsigned bx = k->tile ? 16 : 256, by = k->tile ? 16 : 1;
             CHK(cuMemsetD32(dC, 0, (size_t)n * n));
             CHK(cuLaunchKernel(k->f, gx, gy, 1, bx, by, 1, 0, NULL, args, NULL));

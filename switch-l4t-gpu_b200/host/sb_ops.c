@@ -9,13 +9,6 @@
 #define DP(p) ((CUdeviceptr)(uintptr_t)(p))
 #define ALIGNED16(p) ((((uintptr_t)(p)) & 15) == 0)
 
-static int occupancy(sb_ctx *c, sb_fn_id f, int block, size_t smem) {
-    int n = 1;
-    /* resolve the function through a zero-size launch */
-    if (sb_launch(c, f, 0, 0, block, 0, NULL, NULL, 0)) return 1;
-    if (cuOccupancyMaxActiveBlocksPerMultiprocessor(&n, c->fn[f], block, smem) != CUDA_SUCCESS || n < 1) n = 1;
-    return n;
-}
 
 /* ------------------------------------------------------------------ SGEMM */
 int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
@@ -27,10 +20,10 @@ int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K,
     const int m = row1 - row0;
     if (m == 0 || N == 0) return 0;
     CUdeviceptr a = DP(A + (size_t)row0 * K), b = DP(B), cc = DP(C + (size_t)row0 * N);
+    /* one CTA per 128x128 tile (two resident per SM); the kernel's tile loop
+     * covers the rest if the count ever exceeds the grid limit */
     const long tiles = (long)CEIL_DIV(m, 128) * CEIL_DIV(N, 128);
-    static __thread int occ = 0;
-    if (!occ) occ = occupancy(c, F_SGEMM_B200, 256, 0);
-    long grid = tiles < (long)c->sms * occ ? tiles : (long)c->sms * occ;
+    const long grid = tiles < 0x7fffffffL ? tiles : 0x7fffffffL;
     void *args[] = {&a, &b, &cc, (void *)&m, &N, &K};
     return sb_launch(c, F_SGEMM_B200, (unsigned)grid, 1, 256, 0, (CUstream)stream, args, 0);
 }

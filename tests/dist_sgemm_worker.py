@@ -1,0 +1,55 @@
+"""Worker for the multi-GPU SGEMM test (run under torch.distributed.run,
+one rank per GPU, NCCL): every rank computes its row panel with the CUDA
+kernel, the panels are all-gathered, and each rank checks the full C
+against the oracle on sampled rows plus a Freivalds check of the whole
+product.  Exit status 0 = all ranks agree with the oracle."""
+import datetime
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(os.path.dirname(HERE), "switch-l4t-gpu_b200"))
+sys.path.insert(0, HERE)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import orc  # noqa: E402
+import sb200  # noqa: E402
+import sgemm_dist  # noqa: E402
+
+
+def main():
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    sb200.init(local)
+    bad = 0
+    try:
+        for ci, (M, N, K, chunks) in enumerate([(1000, 384, 1002, 1), (2048, 512, 256, 3), (257, 129, 67, 2)]):
+            A = sb200.synth_uniform(M * K, -1.0, 1.0, 10 + ci).reshape(M, K)
+            B = sb200.synth_uniform(K * N, -1.0, 1.0, 20 + ci).reshape(K, N)
+            ps = sgemm_dist.PanelSgemm(M, N, K, chunks=chunks)
+            Ap = torch.from_numpy(A[ps.row0:ps.row1].copy()).to(dev)
+            Bd = torch.from_numpy(B).to(dev)
+            C = ps(Ap, Bd).cpu().numpy()
+            rows = sorted(set([0, M - 1] + list(range(rank, M, max(1, M // 16)))))
+            want = orc.sgemm(A, B)
+            rel = np.linalg.norm(C[rows] - want[rows]) / np.linalg.norm(want[rows])
+            fr = orc.freivalds(A, B, np.ascontiguousarray(C))
+            ok = rel <= 1e-5 and fr <= 1e-5
+            print(f"rank {rank} case {ci} M={M} N={N} K={K} chunks={chunks}: rel {rel:.2e} freivalds {fr:.2e} "
+                  f"{'ok' if ok else 'BAD'}", flush=True)
+            bad += 0 if ok else 1
+        flag = torch.tensor([bad], device=dev)
+        dist.all_reduce(flag)
+        bad = int(flag.item())
+    finally:
+        dist.destroy_process_group()
+    sys.exit(1 if bad else 0)
+
+
+if __name__ == "__main__":
+    main()

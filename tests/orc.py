@@ -30,6 +30,8 @@ def oracle():
     L.orc_h2f.argtypes = [ctypes.c_uint16]
     L.orc_sgemm_rows.argtypes = [P, P, P, I, I, I, I, I, I]
     L.orc_sgemm_rows.restype = None
+    L.orc_sgemm_bad_cells.argtypes = [P, P, ctypes.c_size_t]
+    L.orc_sgemm_bad_cells.restype = I
     L.orc_freivalds.argtypes = [P, P, P, I, I, I, ctypes.c_uint64, I]
     L.orc_freivalds.restype = D
     L.orc_gemv_f32.argtypes = [P, P, P, P, I, I, I]
@@ -66,6 +68,12 @@ def sgemm(A, B, row0=0, row1=None, nthreads=NTHREADS):
     C = np.zeros((M, N), dtype=np.float32)
     oracle().orc_sgemm_rows(_f32p(A), _f32p(B), _f32p(C), M, N, K, row0, row1, nthreads)
     return C
+
+
+def sgemm_bad_cells(C, ref):
+    """Cells outside the harness tolerance (gpu_workload.c:99-101)."""
+    C, ref = np.ascontiguousarray(C, dtype=np.float32), np.ascontiguousarray(ref, dtype=np.float32)
+    return oracle().orc_sgemm_bad_cells(_f32p(C), _f32p(ref), C.size)
 
 
 def freivalds(A, B, C, seed=7):

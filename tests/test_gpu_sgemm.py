@@ -46,7 +46,7 @@ def test_dropin_stock_geometry(cuda_dev, swmod, name, tile, n):
     ref = orc.sgemm(A, B)
     assert np.isfinite(C).all()
     assert _rel_frob(C, ref) <= REL_FROB
-    assert orc.oracle().orc_sgemm_bad_cells(C.ctypes.data, ref.ctypes.data, C.size) == 0
+    assert orc.sgemm_bad_cells(C, ref) == 0
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 256), (33, 70, 129)])
