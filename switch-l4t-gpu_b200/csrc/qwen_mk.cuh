@@ -3,33 +3,42 @@
 //
 // Why: a decode step is ~120 dependent matvec stages; as separate kernels
 // each pays launch, ramp-up and a chain of dependent global round trips
-// (measured ~6-13 us per kernel).  Here every stage is separated by a
-// grid-wide barrier instead, and the weights -- which never depend on the
-// activations -- are fetched ahead of the barriers:
+// (measured ~6-13 us per kernel).  Here the stages run back to back inside
+// one launch and the weights -- which never depend on the activations --
+// are fetched ahead of time:
 //   * each warp copies its rows of the NEXT stage into its own shared-memory
-//     region with cp.async right after finishing the current stage, i.e.
-//     while it waits at the barrier, so after the barrier the weights are
-//     already on chip;
-//   * thread 0 of each CTA issues an L2 bulk prefetch of its whole slice of
-//     the next layer (~200 KB per CTA, ~30 MB in total) so HBM streams
-//     continuously underneath the barrier latency chain.
+//     region with TMA bulk copies as soon as its current rows are consumed,
+//     so the copies land while the stage's inputs are still being produced;
+//   * one lane issues L2 bulk prefetches of this CTA's slice of the next
+//     layer (~200 KB per CTA, ~30 MB in total) in five pieces, so HBM streams
+//     underneath the dependency chain.
+//
+// Stage hand-off without grid barriers: every activation value a stage
+// produces is stored as one 8-byte word (float bits | epoch << 32) with a
+// single relaxed 64-bit store; the consumer polls exactly the words it needs
+// until their epoch is the current one.  A 64-bit aligned access is
+// single-copy atomic, so a word whose epoch matches carries its value: no
+// fence, no counter, one round trip from producer store to consumer load.
+// Epoch = (step sequence number << 7) | (layer * 5 + stage + 1); the
+// sequence number advances once per step, so stale words never match.  A
+// buffer is rewritten only after every consumer of its previous contents
+// has finished (each stage needs ALL outputs of the one before, which in
+// turn were computed from the buffer), so one buffer per quantity suffices.
+//
 // Stages per layer (each CTA owns a contiguous block of rows of every matrix):
-//   S1 RMSNorm(x) -> QKV rows (RoPE pairs) + bias + RoPE -> q, K/V cache
-//   S2 attention partials: (head, T-split) items, split-local softmax
-//   S3 combine partials -> att; O rows; x += O att
-//   S4 RMSNorm(x) -> gate/up row pairs -> SwiGLU -> hid
-//   S5 down rows (split-K over warps); x += down hid
-// then final RMSNorm -> LM head rows (cp.async ring per warp) -> logits +
-// argmax, and the step finalisation (next token, position).
+//   S1 RMSNorm(x) -> QKV rows (RoPE pairs) + bias + RoPE -> q, k, v words
+//      (and k, v into the KV cache for later steps)
+//   S2 attention partials: (head, T-split) items, one per CTA; the cached
+//      K/V rows are loaded before q arrives
+//   S3 combine partials -> att; O rows; x += O att  -> x words (own rows)
+//   S4 RMSNorm(x) -> gate/up row pairs -> SwiGLU -> hid words
+//   S5 down rows (split-K over warp pairs); x += down hid -> x words
+// then final RMSNorm -> LM head rows (bulk-copy ring per warp) -> logits +
+// argmax; CTA 0 counts the arrivals and finalises the step (next token,
+// position, sequence number).
 //
-// Every input of a stage that does not depend on this step's activations
-// (weights, norm gains, biases, RoPE cos/sin) is requested BEFORE the
-// barrier that precedes the stage, so after it only the activations
-// themselves cross L2 (one round trip).  Each CTA keeps its own residual
-// rows on chip, so the residual adds need no re-read.
-//
-// Barrier waits are bounded: after SPIN_LIMIT polls the kernel sets *err,
-// drains its own copies and returns; the host reports the error.
+// Waits are bounded: after LL_SPIN_LIMIT polls the kernel sets *err, drains
+// its own bulk copies and returns; the host reports the error.
 #pragma once
 #include "sb_attn.cuh"
 #include "sb_finalize.cuh"
@@ -54,43 +63,42 @@ constexpr int CPR_D = FC / 8;         // chunks per K=4864 row (608)
 constexpr int WHEAD = 6 * C * 2;      // per-warp head slot: 6 rows of 896 fp16 (S1, S4, S5, LM head)
 constexpr int WREG = WHEAD + C;       // + tail slot for the O half-row (896 B): 11648 B per warp
 constexpr int LM_NB = 3;              // LM-head rows in flight per warp
-constexpr long SPIN_LIMIT = 1L << 22; // barrier polls (~seconds) before giving up
+constexpr int SPLITS_MAX = SB_MK_SPLITS_MAX;
+constexpr int PW = HD + 2;            // words per attention partial: o[64], m, l
+// flagged-word layout (u64 words)
+constexpr int LL_X = 0, LL_QKV = LL_X + C, LL_HID = LL_QKV + QKV, LL_PART = LL_HID + FC;
+constexpr int LL_WORDS = LL_PART + NH * SPLITS_MAX * PW;
+static_assert(LL_WORDS == SB_MK_LL_WORDS, "flagged-word layout");
+static_assert(LL_QKV % 2 == 0 && LL_HID % 2 == 0 && LL_PART % 2 == 0 && PW % 2 == 0, "pairs stay 16-byte aligned");
+constexpr long LL_SPIN_LIMIT = 1L << 21;  // polls (~a second) before giving up
+constexpr int HID_PAIRS = (FC / 2 + THREADS - 1) / THREADS;  // hid word pairs per thread (5)
+
+typedef unsigned long long u64;
 
 // Typed view of SbMkParams.
 struct Params {
     const unsigned short *w; // weight file image
     float *kv;               // [2][NL][ctx][KVD]
-    float *x;                // residual [C]
-    float *q;                // [C]
-    float *part;             // attention partials [NH * splits][HD + 2]
-    float *hid;              // [FC]
+    u64 *ll;                 // flagged words
     float *logits;           // [V]
     SbStep *st;
     int *tokens;
-    unsigned *bar;           // grid barrier counter, zero at launch
-    int *err;                // set on a barrier timeout
+    unsigned *sync;          // [0] step sequence number, [1] LM-head arrivals
+    int *err;                // set on a wait timeout
     unsigned long long *trace;
     int ctx_cap;
     int with_logits;
-    int splits;              // attention T-splits per head (<= gridDim.x / NH)
+    int splits;              // attention T-splits per head (<= SPLITS_MAX)
     int score_cap;           // positions per split the score buffer holds
     SB_DEV explicit Params(const SbMkParams &r)
-        : w((const unsigned short *)r.w), kv((float *)r.kv), x((float *)r.x), q((float *)r.q),
-          part((float *)r.part), hid((float *)r.hid), logits((float *)r.logits), st((SbStep *)r.st),
-          tokens((int *)r.tokens), bar((unsigned *)r.bar), err((int *)r.err),
-          trace((unsigned long long *)r.trace), ctx_cap(r.ctx_cap),
-          with_logits(r.with_logits), splits(r.splits), score_cap(r.score_cap) {}
+        : w((const unsigned short *)r.w), kv((float *)r.kv), ll((u64 *)r.ll), logits((float *)r.logits),
+          st((SbStep *)r.st), tokens((int *)r.tokens), sync((unsigned *)r.sync), err((int *)r.err),
+          trace((unsigned long long *)r.trace), ctx_cap(r.ctx_cap), with_logits(r.with_logits),
+          splits(r.splits), score_cap(r.score_cap) {}
 };
 
 // ------------------------------------------------------------------ PTX helpers
 SB_DEV unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
-SB_DEV void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-SB_DEV void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-SB_DEV void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-template <int N>
-SB_DEV void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 SB_DEV unsigned long long globaltimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -102,10 +110,51 @@ SB_DEV unsigned ld_acquire(const unsigned *p) {
     return v;
 }
 
+// ---- flagged words
+SB_DEV u64 ll_word(float v, unsigned e) { return ((u64)e << 32) | __float_as_uint(v); }
+SB_DEV void ll_put(u64 *p, float v, unsigned e) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(ll_word(v, e)) : "memory");
+}
+SB_DEV u64 ll_get(const u64 *p) {
+    u64 v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+SB_DEV void ll_get2(const u64 *p, u64 &a, u64 &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+SB_DEV bool ll_is(u64 w, unsigned e) { return (unsigned)(w >> 32) == e; }
+SB_DEV float ll_val(u64 w) { return __uint_as_float((unsigned)w); }
+// Called after a poll found stale words: every 64 polls stop if another CTA
+// gave up, or give up after the limit.  (A back-off sleep between polls was
+// measured slower: the added detection delay outweighs the L2 traffic saved.)
+SB_DEV bool ll_keep_polling(long spin, int *err) {
+    if ((spin & 63) != 63) return true;
+    if (*(volatile int *)err) return false;
+    if (spin > LL_SPIN_LIMIT) {
+        atomicExch(err, 3);
+        return false;
+    }
+    return true;
+}
+// The pair of words at p (16-byte aligned) once both carry epoch e.
+SB_DEV bool ll_wait2(const u64 *p, unsigned e, float &a, float &b, int *err) {
+    for (long spin = 0;; spin++) {
+        u64 w0, w1;
+        ll_get2(p, w0, w1);
+        if (ll_is(w0, e) && ll_is(w1, e)) {
+            a = ll_val(w0);
+            b = ll_val(w1);
+            return true;
+        }
+        if (!ll_keep_polling(spin, err)) return false;
+    }
+}
+
 // ---- TMA bulk staging: one lane per warp issues cp.async.bulk (global ->
 // shared, completing on an mbarrier) for whole row segments.  Bulk copies
 // run on the TMA engine, so they do not queue in front of the ordinary
-// loads (activations, barrier polls) of the stage that follows.
+// loads (activation words, polls) of the stage that follows.
 SB_DEV void mbar_init(uint64_t *mb, unsigned count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(mb)), "r"(count) : "memory");
 }
@@ -130,58 +179,6 @@ SB_DEV bool mbar_wait(uint64_t *mb, unsigned ph) {
         if (done) return true;
     }
     return false;
-}
-
-// Copy `nchunks` 16-byte chunks of one weight row (starting at chunk c0)
-// into shared memory, warp-cooperatively.
-SB_DEV void warp_copy_row(void *dst, const unsigned short *row, int c0, int nchunks) {
-    const int lane = threadIdx.x & 31;
-    const uint4 *src = reinterpret_cast<const uint4 *>(row) + c0;
-    uint4 *d = reinterpret_cast<uint4 *>(dst);
-    for (int c = lane; c < nchunks; c += 32) cp_async16(d + c, src + c);
-}
-
-// Grid-wide barrier, split in two so a CTA can issue its prefetches for the
-// coming stages in between (that time is spent waiting anyway).
-// grid_arrive: all of this CTA's writes are ordered before a release
-// increment of the counter.  grid_wait: returns false on timeout (after
-// setting *err).  `target` = arrivals to wait for (k * gridDim.x at the k-th
-// barrier).
-// The arrive and the polling are done by POLLER, the first lane of the last
-// warp: that warp issues its own prefetches only after the wait, so the
-// poll starts as soon as the CTA has arrived.
-constexpr int POLLER = THREADS - 32;
-SB_DEV void grid_arrive(const Params &p, unsigned target) {
-    __syncthreads();
-    if (threadIdx.x == POLLER) {
-        if (p.trace) {
-            const unsigned idx = target / gridDim.x;  // 1-based barrier number
-            if (idx < 128) p.trace[((size_t)blockIdx.x * 128 + idx) * 2] = globaltimer();
-        }
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-    }
-}
-SB_DEV bool grid_wait(const Params &p, unsigned target, int *abort_s) {
-    if (threadIdx.x == POLLER) {
-        long spins = 0;
-        while (ld_acquire(p.bar) < target) {
-            if ((++spins & 255) == 0) {
-                if (*(volatile int *)p.err) break;
-                if (spins > SPIN_LIMIT) { atomicExch(p.err, 1); break; }
-            }
-        }
-        *abort_s = *(volatile int *)p.err;
-        if (p.trace) {
-            const unsigned idx = target / gridDim.x;
-            if (idx < 128) p.trace[((size_t)blockIdx.x * 128 + idx) * 2 + 1] = globaltimer();
-        }
-    }
-    __syncthreads();
-    return *abort_s == 0;
-}
-SB_DEV bool grid_sync(const Params &p, unsigned target, int *abort_s) {
-    grid_arrive(p, target);
-    return grid_wait(p, target, abort_s);
 }
 
 // Contiguous share [lo, hi) of n units for CTA b of g.
@@ -210,17 +207,14 @@ SB_DEV void smem_rows_dot(const uint4 *base, int stride, int nvalid, const float
     for (int r = 0; r < R; r++) out[r] = f2_sum(acc[r]);
 }
 
-// dot of one smem row (K/8 chunks) with the split x planes, lane-strided,
-// chunk range [c0, c1) of the plane index.
-SB_DEV float smem_row_dot(const uint4 *row, const float4 *lo, const float4 *hi, int c0, int c1, int row_c0) {
-    float acc = 0.0f;
-    for (int c = c0 + (threadIdx.x & 31); c < c1; c += 32) acc = dot_chunk(WH(), row[c - row_c0], lo[c], hi[c], acc);
-    return acc;
+// Element i of a K-vector lives in plane (i%8)<4 ? lo : hi, float (i/8)*4 + i%4.
+SB_DEV float *plane_elem(float4 *lo, float4 *hi, int i) {
+    return reinterpret_cast<float *>((i & 7) < 4 ? lo : hi) + (i >> 3) * 4 + (i & 3);
 }
 
 // RMSNorm from registers: thread t < C/2 holds elements (2t, 2t+1) of x in
 // xv and the two fp16 gains in gw (packed); writes x*inv*g into the split
-// planes (element i lives in plane (i%8)<4 ? lo : hi, float (i/8)*4 + i%4).
+// planes.
 SB_DEV void rms_regs(float2 xv, unsigned gw, float4 *lo, float4 *hi, float *red, float eps) {
     const int t = threadIdx.x;
     const bool act = t < C / 2;
@@ -230,35 +224,15 @@ SB_DEV void rms_regs(float2 xv, unsigned gw, float4 *lo, float4 *hi, float *red,
     if (act) {
         const float g0 = h2f_ftz((unsigned short)(gw & 0xffffu)), g1 = h2f_ftz((unsigned short)(gw >> 16));
         const float2 y = make_float2(__fmul_rn(__fmul_rn(xv.x, inv), g0), __fmul_rn(__fmul_rn(xv.y, inv), g1));
-        const int i = 2 * t, c = i / 8, j = i % 8;
-        float *plane = reinterpret_cast<float *>(j < 4 ? lo : hi);
-        *reinterpret_cast<float2 *>(plane + c * 4 + (j % 4)) = y;
+        *reinterpret_cast<float2 *>(plane_elem(lo, hi, 2 * t)) = y;
     }
 }
 
-// Stage RMSNorm(x) * g into split planes (x read through L2: other CTAs wrote it).
-SB_DEV void stage_rms(const float *x, const unsigned short *g, float4 *lo, float4 *hi, float *red, float eps) {
-    float s = 0.0f;
-    for (int i = threadIdx.x; i < C; i += blockDim.x) {
-        const float v = __ldcg(x + i);
-        s = fmaf(v, v, s);
-    }
-    s = block_sum(s, red);
-    const float inv = 1.0f / sqrtf(__fdiv_rn(s, (float)C) + eps);
-    for (int c = threadIdx.x; c < CPR; c += blockDim.x) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = __fmul_rn(__fmul_rn(__ldcg(x + 8 * c + j), inv), h2f_ftz(g[8 * c + j]));
-        lo[c] = make_float4(v[0], v[1], v[2], v[3]);
-        hi[c] = make_float4(v[4], v[5], v[6], v[7]);
-    }
-}
-
-// ------------------------------------------------------------------ the kernel
 }  // namespace qmk
 
 // grid: one CTA per SM (cooperative launch, >= 128 CTAs); block qmk::THREADS;
-// dynamic smem: FC*4 + WARPS*WREG + score_cap*4 + (32 + WARPS*64 + WARPS)*4 bytes.
+// dynamic smem: FC*4 + WARPS*WREG + score_cap*4
+//               + (32 + WARPS*64 + WARPS + NH*SPLITS_MAX*2)*4 bytes.
 extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(const SbMkParams raw) {
     using namespace qmk;
     const Params p(raw);
@@ -270,9 +244,9 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     float *scores = reinterpret_cast<float *>(wbase + (size_t)WARPS * WREG);
     // float2/float4 accesses follow: keep every region 16-byte aligned
     float *red = scores + ((p.score_cap + 3) & ~3);  // 32 floats
-    float *opart = red + 32;            // WARPS x HD per-warp partial P.V
-    float *ksum = opart + WARPS * HD;   // WARPS floats: split-K partials / per-warp softmax sums
-    __shared__ int abort_s;
+    float *opart = red + 32;                          // WARPS x HD per-warp partial P.V
+    float *ksum = opart + WARPS * HD;                 // WARPS floats: split-K partials / per-warp softmax sums
+    float *mlv = ksum + WARPS;                        // NH*SPLITS_MAX (m, l) pairs of the partials
     __shared__ float wmax_s[WARPS], xown[8];
     __shared__ unsigned long long best_s;
     __shared__ __align__(8) uint64_t mbar[WARPS][2 + LM_NB];
@@ -281,14 +255,17 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     unsigned char *wreg = wbase + (size_t)warp * WREG;
     const uint4 *wreg4 = reinterpret_cast<const uint4 *>(wreg);
-    unsigned target = 0;
-    if (tid == 0) abort_s = 0;
     if (sb_step_idle(p.st)) return;  // uniform: every CTA reads the same state
     if (lane == 0)
         for (int i = 0; i < 2 + LM_NB; i++) mbar_init(&mbar[warp][i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
     if (p.trace && tid == 0) p.trace[(size_t)b * 256] = globaltimer();  // slot 0: start
+    const unsigned seq = p.sync[0];
+    auto epoch = [&](int l, int s) { return (seq << 7) | (unsigned)(l * 5 + s + 1); };
+    auto stamp = [&](int l, int s, int which) {  // which 0: inputs ready, 1: outputs written
+        if (p.trace && tid == 0) p.trace[(size_t)b * 256 + 1 + 2 * (l * 5 + s) + which] = globaltimer();
+    };
     const int pos = p.st->pos, T = pos + 1;
     const int tok = p.tokens[pos];
     const float eps = 1e-6f;
@@ -296,6 +273,8 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     const float *cosT = reinterpret_cast<const float *>(reinterpret_cast<const char *>(p.w) + OFF_COS);
     const float *sinT = reinterpret_cast<const float *>(reinterpret_cast<const char *>(p.w) + OFF_SIN);
     const bool xact = tid < C / 2;  // holds x elements (2 tid, 2 tid + 1) in RMS stages
+    u64 *const llx = p.ll + LL_X, *const llqkv = p.ll + LL_QKV, *const llhid = p.ll + LL_HID;
+    u64 *const llpart = p.ll + LL_PART;
 
     // per-CTA shares (static over the step)
     int qp0, qp1, or0, or1, gp0, gp1;
@@ -304,15 +283,14 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     share(FC, b, G, gp0, gp1);       // gate/up pairs
     // attention T-splits: ~48 positions per item (a warp holds up to 4
     // positions' K/V in registers), at most p.splits per head
-    const int nsplit = max(1, min(p.splits, (T + 47) / 48));
+    const int nsplit = max(1, min(min(p.splits, SPLITS_MAX), (T + 47) / 48));
     const int slen = (T + nsplit - 1) / nsplit;
 
     auto layer_ptr = [&](int l) { return p.w + (LBASE / 2) + (long)l * (LSTRIDE / 2); };
 
     // L2 prefetch of this CTA's slices of layer l, in five pieces of ~40 KB
     // (one per stage) so the weight stream is spread evenly over the layer
-    // instead of bursting in front of the latency-critical barrier and
-    // activation traffic.  Issued by one lane (not the barrier poller).
+    // instead of bursting in front of the latency-critical activation traffic.
     auto prefetch_piece = [&](int l, int piece) {
         if (l >= NL) return;
         const unsigned short *L = layer_ptr(l);
@@ -337,16 +315,23 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     // ---- weight staging into the warp's region by TMA bulk copies (lane 0
     // issues; the warp waits on the slot's mbarrier before reading)
     // mbar[warp][0]: head slot (S1, S4, S5 rows); [1]: tail slot (O half-row);
-    // [2 + k]: LM-head ring slot k.  `phase` bit i = parity to wait for next.
-    unsigned phase = 0;
+    // [2 + k]: LM-head ring slot k.  `phase` bit i = parity to wait for next;
+    // `pend` bit i (lane 0) = a copy into slot i has not been waited for.
+    unsigned phase = 0, pend = 0;
     uint64_t *mb = mbar[warp];
+    // Lane 0 orders the warp's earlier generic accesses of its region before
+    // the async-proxy writes of the copies it issues next (once per batch).
+    auto fence_async = [&]() {
+        if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    };
     auto issue_begin = [&](int i, unsigned bytes) {  // lane 0 only
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of the slot
         mbar_expect_tx(&mb[i], bytes);
+        pend |= 1u << i;
     };
     auto wait_slot = [&](int i) {
         if (!mbar_wait(&mb[i], (phase >> i) & 1u) && lane == 0) atomicExch(p.err, 2);
         phase ^= 1u << i;
+        pend &= ~(1u << i);
     };
     auto copy_s1 = [&](int l) {  // warp w < npairs: pair qp0 + w, rows r, r+32
         if (lane != 0) return;
@@ -368,7 +353,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     };
     // gate/up pairs gp0 + warp + 16k, k < 3, rows (gate_k, up_k): the byte
     // count of all pairs is announced with the first piece, then one pair is
-    // issued per stage (S1 arrive, S2, S3) to spread the traffic
+    // issued per stage (S1, S2, S3) to spread the traffic
     auto copy_s4_piece = [&](int l, int k) {
         if (lane != 0) return;
         const int npair = min(3, max(0, (gp1 - (gp0 + warp) + WARPS - 1) / WARPS));
@@ -386,25 +371,35 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         issue_begin(0, r < or1 ? FC : 0);
         if (r < or1) bulk_g2s(wreg, layer_ptr(l) + L_DOWN + (long)r * FC + half * (FC / 2), FC, &mb[0]);
     };
-    // Split-K (2 warps per row) reduction + residual update of this CTA's rows.
-    auto resid_update = [&](float a) {
+    // Split-K (2 warps per row) reduction + residual update of this CTA's
+    // rows, published as x words of epoch e.
+    auto resid_update = [&](float a, unsigned e) {
         if (lane == 0) ksum[warp] = a;
         __syncthreads();
         if (tid < or1 - or0) {
             const float y = ksum[2 * tid] + ksum[2 * tid + 1];
             const float xn = __fadd_rn(xown[tid], y);
             xown[tid] = xn;
-            p.x[or0 + tid] = xn;
+            ll_put(llx + or0 + tid, xn, e);
         }
     };
+    // x words of epoch e -> xv (thread t < C/2: elements 2t, 2t+1); uniform
+    // result: false when this or another CTA gave up.
+    float2 xv = make_float2(0.f, 0.f);
+    auto wait_x = [&](unsigned e) {
+        bool ok = true;
+        if (xact) ok = ll_wait2(llx + 2 * tid, e, xv.x, xv.y, p.err);
+        return !__syncthreads_or(!ok);
+    };
+    bool aborted = false;
 
     // ---- prologue: this CTA's residual rows start as the embedding
     if (tid < or1 - or0) xown[tid] = h2f_ftz(emb[(long)tok * C + or0 + tid]);
     if (prefetcher)
         for (int piece = 0; piece < 5; piece++) prefetch_piece(0, piece);
+    fence_async();
     copy_s1(0);
-    // layer-0 S1 input: the embedding row (constant: no barrier needed)
-    float2 xv = make_float2(0.f, 0.f);
+    // layer-0 S1 input: the embedding row (constant: nothing to wait for)
     if (xact) {
         const unsigned e2 = *reinterpret_cast<const unsigned *>(emb + (long)tok * C + 2 * tid);
         xv = make_float2(h2f_ftz((unsigned short)(e2 & 0xffffu)), h2f_ftz((unsigned short)(e2 >> 16)));
@@ -425,22 +420,14 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         }
     };
     s1_consts(0);
-    bool pending_s1 = false;
 
     for (int l = 0; l < NL; l++) {
         const unsigned short *L = layer_ptr(l);
         float *kc = p.kv + (long)l * p.ctx_cap * KVD;
         float *vc = p.kv + (long)(NL + l) * p.ctx_cap * KVD;
-        // ================= S1: RMSNorm -> QKV -> RoPE -> q / cache
-        if (l > 0) {
-            if (!grid_wait(p, target, &abort_s)) break;  // arrival was at the end of S5
-            if (pending_s1) {  // the poller's warp: its S1 copies and constants now
-                copy_s1(l);
-                s1_consts(l);
-                pending_s1 = false;
-            }
-            if (xact) xv = __ldcg(reinterpret_cast<const float2 *>(p.x) + tid);
-        }
+        // ================= S1: RMSNorm -> QKV -> RoPE -> q, k, v words
+        if (l > 0 && !wait_x(epoch(l - 1, 4))) { aborted = true; break; }
+        stamp(l, 0, 0);
         rms_regs(xv, gw1, xlo, xhi, red, eps);
         __syncthreads();
         if (prefetcher) {
@@ -468,52 +455,97 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                     y0 = o0;
                     y1 = o1;
                 }
-                if (h < NH) { p.q[r0] = y0; p.q[r1] = y1; }
-                else if (h < NH + NKV) { kc[(long)pos * KVD + r0 - C] = y0; kc[(long)pos * KVD + r1 - C] = y1; }
-                else { vc[(long)pos * KVD + r0 - C - KVD] = y0; vc[(long)pos * KVD + r1 - C - KVD] = y1; }
+                const unsigned e = epoch(l, 0);
+                ll_put(llqkv + r0, y0, e);
+                ll_put(llqkv + r1, y1, e);
+                if (h >= NH + NKV) { vc[(long)pos * KVD + r0 - C - KVD] = y0; vc[(long)pos * KVD + r1 - C - KVD] = y1; }
+                else if (h >= NH) { kc[(long)pos * KVD + r0 - C] = y0; kc[(long)pos * KVD + r1 - C] = y1; }
             }
         }
-        target += G;
-        grid_arrive(p, target);
-        // O rows (tail slot) and gate/up rows (head slot; S1's rows are
-        // consumed) arrive while the barriers, attention and O run; the
-        // poller's warp issues its copies after the wait
-        if (warp != WARPS - 1) { copy_s3(l); copy_s4_piece(l, 0); }
+        stamp(l, 0, 1);
+        // O rows (tail slot) and two gate/up pairs (head slot: S1's rows are
+        // consumed) stream in while attention runs.  A CTA with an attention
+        // item issues them after it: issuing bulk copies stalls the issuing
+        // lanes for ~1.5 us, and the item is on the critical path.
+        const bool has_item = b < NH * nsplit;
+        auto issue_s3_s4 = [&]() {
+            fence_async();
+            copy_s3(l);
+            copy_s4_piece(l, 0);
+            copy_s4_piece(l, 1);
+            if (prefetcher) prefetch_piece(l + 1, 1);
+        };
+        if (!has_item) issue_s3_s4();
         // ================= S2: attention partials; a warp per position, K and V
-        // rows loaded together so one L2 round trip serves scores and P.V
-        if (!grid_wait(p, target, &abort_s)) break;
-        if (warp == WARPS - 1) { copy_s3(l); copy_s4_piece(l, 0); }
-        copy_s4_piece(l, 1);
-        if (prefetcher) prefetch_piece(l + 1, 1);
+        // rows loaded together so one round trip serves scores and P.V
+        const unsigned e_qkv = epoch(l, 0);
         for (int item = b; item < NH * nsplit; item += G) {
             const int h = item / nsplit, s = item % nsplit, g = h / (NH / NKV);
             const int t0 = s * slen, t1 = min(T, t0 + slen), n = max(0, t1 - t0);
-            const float2 q2 = __ldcg(reinterpret_cast<const float2 *>(p.q + h * HD) + lane);
-            // each warp keeps up to 4 positions' scores and V rows in registers
-            float sc[4];
-            float2 vv[4];
+            const u64 *kcur = llqkv + C + g * HD + 2 * lane, *vcur = llqkv + C + KVD + g * HD + 2 * lane;
+            __syncthreads();  // the previous item's readers of opart are done
+            // each warp keeps up to 4 positions' K and V rows in registers;
+            // cached positions (< pos) are requested before q is awaited
+            float2 kk[4], vv[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const int j = warp + WARPS * k;
-                sc[k] = -1e30f;
-                vv[k] = make_float2(0.f, 0.f);
-                if (j < n) {
-                    const float2 k2 = __ldcg(reinterpret_cast<const float2 *>(kc + (long)(t0 + j) * KVD + g * HD) + lane);
-                    vv[k] = __ldcg(reinterpret_cast<const float2 *>(vc + (long)(t0 + j) * KVD + g * HD) + lane);
-                    sc[k] = warp_sum(fmaf(q2.x, k2.x, q2.y * k2.y)) * 0.125f;
+                const int t = t0 + warp + WARPS * k;
+                kk[k] = vv[k] = make_float2(0.f, 0.f);
+                if (t < t1 && t < pos) {
+                    kk[k] = __ldcg(reinterpret_cast<const float2 *>(kc + (long)t * KVD + g * HD) + lane);
+                    vv[k] = __ldcg(reinterpret_cast<const float2 *>(vc + (long)t * KVD + g * HD) + lane);
                 }
             }
-            // positions beyond 64 per item (long contexts): scores via smem, V re-read
+            // one warp waits for q_h and (when this item holds pos) the current
+            // k, v rows and shares them through shared memory: sixteen warps
+            // polling the same hot words slow down their producers' stores
+            float2 *qkv_s = reinterpret_cast<float2 *>(opart);  // q | k | v pairs (opart is free here)
+            bool ok = true;
+            if (warp == 0) {
+                float2 v;
+                ok = ll_wait2(llqkv + h * HD + 2 * lane, e_qkv, v.x, v.y, p.err);
+                qkv_s[lane] = v;
+                if (t1 == T) {
+                    ok = ok && ll_wait2(kcur, e_qkv, v.x, v.y, p.err);
+                    qkv_s[32 + lane] = v;
+                    ok = ok && ll_wait2(vcur, e_qkv, v.x, v.y, p.err);
+                    qkv_s[64 + lane] = v;
+                }
+            }
+            if (__syncthreads_or(!ok)) { aborted = true; break; }
+            const float2 q2 = qkv_s[lane];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (t0 + warp + WARPS * k == pos) {
+                    kk[k] = qkv_s[32 + lane];
+                    vv[k] = qkv_s[64 + lane];
+                }
+            float sc[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                sc[k] = -1e30f;
+                if (warp + WARPS * k < n) sc[k] = warp_sum(fmaf(q2.x, kk[k].x, q2.y * kk[k].y)) * 0.125f;
+            }
+            // positions beyond 64 per item (long contexts): scores via smem, V
+            // re-read (the current position's V word is kept from here)
+            float2 vpos = make_float2(0.f, 0.f);
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) {
-                const float2 k2 = __ldcg(reinterpret_cast<const float2 *>(kc + (long)(t0 + j) * KVD + g * HD) + lane);
+                const int t = t0 + j;
+                float2 k2;
+                if (t == pos) {
+                    k2 = qkv_s[32 + lane];
+                    vpos = qkv_s[64 + lane];
+                } else {
+                    k2 = __ldcg(reinterpret_cast<const float2 *>(kc + (long)t * KVD + g * HD) + lane);
+                }
                 const float d = warp_sum(fmaf(q2.x, k2.x, q2.y * k2.y)) * 0.125f;
                 if (lane == 0) scores[j] = d;
             }
-            __syncwarp();
             float wm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+            __syncwarp();
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) wm = fmaxf(wm, scores[j]);
             if (lane == 0) wmax_s[warp] = wm;
-            __syncthreads();
+            if (__syncthreads_or(!ok)) { aborted = true; break; }
             float m = -1e30f;
 #pragma unroll
             for (int w = 0; w < WARPS; w++) m = fmaxf(m, wmax_s[w]);
@@ -529,9 +561,11 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                 }
             }
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) {
+                const int t = t0 + j;
                 const float e = expf(scores[j] - m);
                 lsum += e;
-                const float2 v2 = __ldcg(reinterpret_cast<const float2 *>(vc + (long)(t0 + j) * KVD + g * HD) + lane);
+                const float2 v2 = t == pos ? vpos
+                                           : __ldcg(reinterpret_cast<const float2 *>(vc + (long)t * KVD + g * HD) + lane);
                 o.x = fmaf(e, v2.x, o.x);
                 o.y = fmaf(e, v2.y, o.y);
             }
@@ -542,56 +576,78 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                 float acc = 0.f;
 #pragma unroll
                 for (int w = 0; w < WARPS; w++) acc += opart[w * HD + tid];
-                float *pp = p.part + (long)(h * p.splits + s) * (HD + 2);
-                pp[tid] = acc;
+                u64 *pw = llpart + (long)(h * SPLITS_MAX + s) * PW;
+                const unsigned e = epoch(l, 1);
+                ll_put(pw + tid, acc, e);
                 if (tid == 0) {
                     float ls = 0.f;
 #pragma unroll
                     for (int w = 0; w < WARPS; w++) ls += ksum[w];
-                    pp[HD] = m;
-                    pp[HD + 1] = ls;
+                    ll_put(pw + HD, m, e);
+                    ll_put(pw + HD + 1, ls, e);
                 }
             }
             __syncthreads();
         }
-        target += G;
-        grid_arrive(p, target);
+        if (aborted) break;
+        stamp(l, 1, 1);
+        if (has_item) issue_s3_s4();
         // ================= S3: combine partials -> att; O rows; x += O att
-        if (!grid_wait(p, target, &abort_s)) break;
         copy_s4_piece(l, 2);
         if (prefetcher) prefetch_piece(l + 1, 2);
-        // 28 (head, 32-dim half) tasks over 16 warps (two per warp at most);
-        // every partial a lane needs for both tasks is requested in one batch
         {
-            float mv[2], lv[2], ov[2][16];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int task = warp + WARPS * u;
-                const int h = task >> 1, d = (task & 1) * 32 + lane;
-                const bool live = task < 2 * NH;
-                const float *base = p.part + (long)(h * p.splits) * (HD + 2);
-                mv[u] = -1e30f;
-                lv[u] = 0.f;
-                if (live && lane < nsplit) {
-                    mv[u] = __ldcg(base + (long)lane * (HD + 2) + HD);
-                    lv[u] = __ldcg(base + (long)lane * (HD + 2) + HD + 1);
-                }
-#pragma unroll
-                for (int s2 = 0; s2 < 16; s2++) ov[u][s2] = (live && s2 < nsplit) ? __ldcg(base + (long)s2 * (HD + 2) + d) : 0.f;
+            const unsigned e = epoch(l, 1);
+            bool ok = true;
+            // (m, l) of every partial into shared memory
+            for (int it = tid; it < NH * nsplit; it += THREADS) {
+                const int h = it / nsplit, s = it % nsplit;
+                float mv, lv;
+                ok = ok && ll_wait2(llpart + (long)(h * SPLITS_MAX + s) * PW + HD, e, mv, lv, p.err);
+                mlv[2 * it] = mv;
+                mlv[2 * it + 1] = lv;
             }
+            // the o words of this thread's dims d = tid and tid + THREADS,
+            // all splits requested before any is checked
+            float ov[2][SPLITS_MAX];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
-                const int task = warp + WARPS * u;
-                if (task >= 2 * NH) break;
-                const int h = task >> 1, d = (task & 1) * 32 + lane;
-                const float M = warp_max(mv[u]);
-                const float wgt = (lane < nsplit) ? expf(mv[u] - M) : 0.f;
-                const float Lsum = warp_sum(wgt * lv[u]);
-                float acc = 0.f;
+                const int d = tid + THREADS * u;
+                if (d >= C) break;
+                const u64 *base = llpart + (long)((d / HD) * SPLITS_MAX) * PW + (d % HD);
+                for (long spin = 0; ok; spin++) {
+                    bool all = true;
 #pragma unroll
-                for (int s2 = 0; s2 < 16; s2++) acc = fmaf(__shfl_sync(SB_FULL, wgt, s2), ov[u][s2], acc);
-                const int c = d / 8, j = d % 8;
-                reinterpret_cast<float *>(j < 4 ? xlo : xhi)[(h * HD / 8 + c) * 4 + (j % 4)] = acc / Lsum;
+                    for (int s = 0; s < SPLITS_MAX; s++) {
+                        ov[u][s] = 0.f;
+                        if (s < nsplit) {
+                            const u64 wv = ll_get(base + (long)s * PW);
+                            all = all && ll_is(wv, e);
+                            ov[u][s] = ll_val(wv);
+                        }
+                    }
+                    if (all) break;
+                    ok = ll_keep_polling(spin, p.err);
+                }
+            }
+            if (__syncthreads_or(!ok)) { aborted = true; break; }
+            stamp(l, 2, 0);
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int d = tid + THREADS * u;
+                if (d >= C) break;
+                const int h = d / HD;
+                float M = -1e30f;
+                for (int s = 0; s < nsplit; s++) M = fmaxf(M, mlv[2 * (h * nsplit + s)]);
+                float acc = 0.f, Lsum = 0.f;
+#pragma unroll
+                for (int s = 0; s < SPLITS_MAX; s++) {
+                    if (s < nsplit) {
+                        const float wgt = expf(mlv[2 * (h * nsplit + s)] - M);
+                        Lsum = fmaf(wgt, mlv[2 * (h * nsplit + s) + 1], Lsum);
+                        acc = fmaf(wgt, ov[u][s], acc);
+                    }
+                }
+                *plane_elem(xlo, xhi, d) = acc / Lsum;
             }
         }
         __syncthreads();
@@ -602,15 +658,14 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             float a[1];
             smem_rows_dot<1>(wreg4 + WHEAD / 16, 0, r < or1 ? 1 : 0, xlo, xhi, half * (CPR / 2), (half + 1) * (CPR / 2),
                              half * (CPR / 2), a);
-            resid_update(warp_sum(a[0]));
+            resid_update(warp_sum(a[0]), epoch(l, 2));
         }
-        target += G;
-        grid_arrive(p, target);
+        stamp(l, 2, 1);
+        // ================= S4: RMSNorm -> gate/up -> SwiGLU -> hid words
         const unsigned gw4 = xact ? *reinterpret_cast<const unsigned *>(L + L_POST + 2 * tid) : 0u;
-        // ================= S4: RMSNorm -> gate/up -> SwiGLU -> hid
-        if (!grid_wait(p, target, &abort_s)) break;
         if (prefetcher) prefetch_piece(l + 1, 3);
-        if (xact) xv = __ldcg(reinterpret_cast<const float2 *>(p.x) + tid);
+        if (!wait_x(epoch(l, 2))) { aborted = true; break; }
+        stamp(l, 3, 0);
         rms_regs(xv, gw4, xlo, xhi, red, eps);
         __syncthreads();
         wait_slot(0);
@@ -620,25 +675,48 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             const int npair = min(3, max(0, (gp1 - (gp0 + warp) + WARPS - 1) / WARPS));
             float a[6];
             smem_rows_dot<6>(wreg4, CPR, 2 * npair, xlo, xhi, 0, CPR, 0, a);
+            const unsigned e = epoch(l, 3);
 #pragma unroll
             for (int k = 0; k < 3; k++) {
                 const float ag = warp_sum(a[2 * k]), au = warp_sum(a[2 * k + 1]);
                 if (k < npair && lane == 0)
-                    p.hid[gp0 + warp + WARPS * k] = __fmul_rn(__fdiv_rn(ag, __fadd_rn(1.0f, expf(-ag))), au);
+                    ll_put(llhid + gp0 + warp + WARPS * k, __fmul_rn(__fdiv_rn(ag, __fadd_rn(1.0f, expf(-ag))), au), e);
             }
         }
-        target += G;
-        grid_arrive(p, target);
-        if (warp != WARPS - 1) copy_s5(l);
+        stamp(l, 3, 1);
+        fence_async();
+        copy_s5(l);
         // ================= S5: down rows (split-K over warp pairs); x += down hid
-        if (!grid_wait(p, target, &abort_s)) break;
-        if (warp == WARPS - 1) copy_s5(l);
         if (prefetcher) prefetch_piece(l + 1, 4);
-        for (int c = tid; c < CPR_D; c += blockDim.x) {
-            xlo[c] = __ldcg(reinterpret_cast<const float4 *>(p.hid) + 2 * c);
-            xhi[c] = __ldcg(reinterpret_cast<const float4 *>(p.hid) + 2 * c + 1);
+        {
+            // hid words into the planes: every pair this thread owns is
+            // requested before any is checked
+            const unsigned e = epoch(l, 3);
+            float2 hv[HID_PAIRS];
+            bool ok = true;
+            for (long spin = 0; ok; spin++) {
+                bool all = true;
+#pragma unroll
+                for (int k = 0; k < HID_PAIRS; k++) {
+                    const int u = tid + THREADS * k;
+                    if (u < FC / 2) {
+                        u64 w0, w1;
+                        ll_get2(llhid + 2 * u, w0, w1);
+                        all = all && ll_is(w0, e) && ll_is(w1, e);
+                        hv[k] = make_float2(ll_val(w0), ll_val(w1));
+                    }
+                }
+                if (all) break;
+                ok = ll_keep_polling(spin, p.err);
+            }
+#pragma unroll
+            for (int k = 0; k < HID_PAIRS; k++) {
+                const int u = tid + THREADS * k;
+                if (u < FC / 2) *reinterpret_cast<float2 *>(plane_elem(xlo, xhi, 2 * u)) = hv[k];
+            }
+            if (__syncthreads_or(!ok)) { aborted = true; break; }
         }
-        __syncthreads();
+        stamp(l, 4, 0);
         wait_slot(0);
         __syncwarp();
         {
@@ -646,25 +724,32 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             float a[1];
             smem_rows_dot<1>(wreg4, 0, r < or1 ? 1 : 0, xlo, xhi, half * (CPR_D / 2), (half + 1) * (CPR_D / 2),
                              half * (CPR_D / 2), a);
-            resid_update(warp_sum(a[0]));
+            resid_update(warp_sum(a[0]), epoch(l, 4));
         }
-        target += G;
-        grid_arrive(p, target);  // waited at the top of the next layer (or before the LM head)
-        if (l + 1 < NL && warp != WARPS - 1) {
+        stamp(l, 4, 1);
+        if (l + 1 < NL) {
+            fence_async();
             copy_s1(l + 1);
             s1_consts(l + 1);
         }
-        if (l + 1 < NL && warp == WARPS - 1) {  // after the poll: the wait at the top of S1
-            pending_s1 = true;
-        }
     }
-    if (abort_s) return;
+    if (aborted) {
+        // drain this warp's bulk copies still in flight, then leave
+        if (lane == 0)
+            for (int i = 0; i < 2 + LM_NB; i++)
+                if ((pend >> i) & 1u) mbar_wait(&mb[i], (phase >> i) & 1u);
+        return;
+    }
     // ================= LM head + argmax
-    const unsigned gwf = xact ? *reinterpret_cast<const unsigned *>(p.w + OFF_LNF / 2 + 2 * tid) : 0u;
-    if (!grid_wait(p, target, &abort_s)) return;
     if (p.with_logits) {
-        if (xact) xv = __ldcg(reinterpret_cast<const float2 *>(p.x) + tid);
+        const unsigned gwf = xact ? *reinterpret_cast<const unsigned *>(p.w + OFF_LNF / 2 + 2 * tid) : 0u;
         if (tid == 0) best_s = 0ull;
+        if (!wait_x(epoch(NL - 1, 4))) {
+            if (lane == 0)
+                for (int i = 0; i < 2 + LM_NB; i++)
+                    if ((pend >> i) & 1u) mbar_wait(&mb[i], (phase >> i) & 1u);
+            return;
+        }
         rms_regs(xv, gwf, xlo, xhi, red, eps);
         __syncthreads();
         int v0, v1;
@@ -672,6 +757,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         // per warp: rows v0 + warp + 16k through a ring of LM_NB row buffers,
         // each filled by a bulk copy completing on its own mbarrier
         unsigned long long best = 0ull;
+        fence_async();
         for (int k = 0; k < LM_NB; k++) {
             const int r = v0 + warp + WARPS * k;
             if (r < v1 && lane == 0) {
@@ -694,30 +780,39 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             __syncwarp();
             const int rn = v0 + warp + WARPS * (k + LM_NB);
             if (rn < v1 && lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 issue_begin(2 + slot, C * 2);
                 bulk_g2s(wreg + slot * C * 2, emb + (long)rn * C, C * 2, &mb[2 + slot]);
             }
         }
         if (lane == 0 && best) atomicMax(&best_s, best);
         __syncthreads();
-        if (tid == 0 && best_s) atomicMax(&p.st->key, best_s);
-        target += G;
-        if (!grid_sync(p, target, &abort_s)) return;
+        if (tid == 0) {
+            if (best_s) atomicMax(&p.st->key, best_s);
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.sync + 1) : "memory");
+        }
+        if (p.trace && tid == 0) p.trace[(size_t)b * 256 + 1 + 2 * 120] = globaltimer();
+        if (b != 0 || tid != 0) return;
+        // CTA 0 finalises once every CTA's argmax is in
+        for (long spin = 0; ld_acquire(p.sync + 1) < (unsigned)G; spin++)
+            if (!ll_keep_polling(spin, p.err)) return;
+        p.sync[1] = 0u;
+    } else if (b != 0 || tid != 0) {
+        return;
     }
     // ================= finalize (one thread of CTA 0), as sb_finalize
-    if (b == 0 && tid == 0) {
-        SbStep *st = p.st;
-        const int pp = st->pos;
-        if (p.with_logits) {
-            const int nxt = argmax_key_index(st->key);
-            st->key = 0ull;
-            if (pp + 1 >= st->n_prompt && pp + 1 < st->n_end) {
-                p.tokens[pp + 1] = nxt;
-                st->n_generated += 1;
-                if (st->stop_on_eos && (nxt == st->eos0 || nxt == st->eos1)) st->done = 1;
-            }
+    SbStep *st = p.st;
+    const int pp = st->pos;
+    if (p.with_logits) {
+        const int nxt = argmax_key_index(st->key);
+        st->key = 0ull;
+        if (pp + 1 >= st->n_prompt && pp + 1 < st->n_end) {
+            p.tokens[pp + 1] = nxt;
+            st->n_generated += 1;
+            if (st->stop_on_eos && (nxt == st->eos0 || nxt == st->eos1)) st->done = 1;
         }
-        st->pos = pp + 1;
-        if (st->pos >= st->n_end - 1) st->done = 1;
     }
+    st->pos = pp + 1;
+    if (st->pos >= st->n_end - 1) st->done = 1;
+    p.sync[0] = seq + 1u;
 }

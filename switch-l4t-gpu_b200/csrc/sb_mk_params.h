@@ -5,24 +5,28 @@
 #ifndef SB_MK_PARAMS_H
 #define SB_MK_PARAMS_H
 
+/* Flagged exchange words (u64 = float bits | epoch << 32) between the
+ * kernel's stages, in this order: residual x[896] | q k v[1152] |
+ * MLP hidden[4864] | attention partials [14 heads][8 splits][66]. */
+#define SB_MK_LL_WORDS (896 + 1152 + 4864 + 14 * 8 * 66)
+#define SB_MK_SPLITS_MAX 8
+
 typedef struct SbMkParams {
-    unsigned long long w;      /* weight file image                        */
-    unsigned long long kv;     /* KV cache [2][layers][ctx][kv_width]      */
-    unsigned long long x;      /* residual                                 */
-    unsigned long long q;      /* query                                    */
-    unsigned long long part;   /* attention partials                       */
-    unsigned long long hid;    /* MLP hidden                               */
-    unsigned long long logits; /* [V]                                      */
-    unsigned long long st;     /* SbStep                                   */
-    unsigned long long tokens; /* token ids                                */
-    unsigned long long bar;    /* grid-barrier counter, zeroed per launch  */
-    unsigned long long err;    /* set to 1 when a barrier wait times out   */
-    unsigned long long trace;  /* 0, or u64 [ctas][128][2] globaltimer stamps:
-                                * (arrive, release) of every grid barrier    */
+    unsigned long long w;      /* weight file image                              */
+    unsigned long long kv;     /* KV cache [2][layers][ctx][kv_width]            */
+    unsigned long long ll;     /* SB_MK_LL_WORDS flagged words, zero at creation */
+    unsigned long long logits; /* [V]                                            */
+    unsigned long long st;     /* SbStep                                         */
+    unsigned long long tokens; /* token ids                                      */
+    unsigned long long sync;   /* u32[2]: step sequence number, LM-head arrivals */
+    unsigned long long err;    /* set nonzero when a wait timed out              */
+    unsigned long long trace;  /* 0, or u64 [ctas][256] globaltimer stamps:
+                                * slot 0 start, 1 + 2k / 2 + 2k inputs ready /
+                                * outputs written of stage k = layer * 5 + s  */
     int ctx_cap;
     int with_logits;
-    int splits;                /* attention T-splits per head              */
-    int score_cap;             /* positions one split's score buffer holds */
+    int splits;                /* attention T-splits per head (<= SPLITS_MAX)    */
+    int score_cap;             /* positions one split's score buffer holds       */
 } SbMkParams;
 
 #endif

@@ -47,9 +47,10 @@ struct sb_engine {
     int n_prompt, n_end;
     /* persistent whole-step kernel (Qwen) */
     int mk;
-    CUdeviceptr bar, err;
+    CUdeviceptr ll, sync, err; /* flagged exchange words; u32[2] seq / arrivals; error flag */
     int mk_splits, mk_score_cap;
     unsigned mk_smem;
+    long mk_steps; /* launches since the flagged words were last cleared */
     CUdeviceptr trace;
 };
 
@@ -57,8 +58,9 @@ struct sb_engine {
 #define MK_WARPS 16
 static unsigned mk_smem_bytes(int score_cap) {
     /* x planes (FC floats) | 16 warp regions of (6 rows + 1/2 row) of 896 fp16 | scores |
-     * red(32) opart(16x64) ksum(16) */
-    return (unsigned)(QW_FC * 4 + MK_WARPS * (6 * QW_C * 2 + QW_C) + score_cap * 4 + (32 + MK_WARPS * 64 + MK_WARPS) * 4);
+     * red(32) opart(16x64) ksum(16) (m, l) of NH x SPLITS_MAX partials */
+    return (unsigned)(QW_FC * 4 + MK_WARPS * (6 * QW_C * 2 + QW_C) + score_cap * 4 +
+                      (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4);
 }
 
 /* ------------------------------------------------------------------ upload */
@@ -218,19 +220,15 @@ static int launch_kernel(sb_engine *e, int l, int which, int with_logits, int pd
 }
 
 static int record_mk(sb_engine *e, int with_logits) {
-    SB_CK(cuMemsetD32Async(e->bar, 0, 1, e->stream));
     SbMkParams prm;
     memset(&prm, 0, sizeof prm);
     prm.w = e->w;
     prm.kv = e->kv;
-    prm.x = e->x;
-    prm.q = e->q;
-    prm.part = e->part;
-    prm.hid = e->hid;
+    prm.ll = e->ll;
     prm.logits = e->logits;
     prm.st = e->step;
     prm.tokens = e->tokens;
-    prm.bar = e->bar;
+    prm.sync = e->sync;
     prm.err = e->err;
     prm.trace = e->trace;
     prm.ctx_cap = e->ctx_cap;
@@ -273,6 +271,7 @@ static int ensure_graph(sb_engine *e, int with_logits) {
 }
 
 static int run_step(sb_engine *e, int with_logits) {
+    e->mk_steps++;
     if (e->flags & SB_FLAG_NO_GRAPH) return record_step(e, with_logits);
     int rc = ensure_graph(e, with_logits);
     if (rc) return rc;
@@ -308,7 +307,7 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
      * shares are sized for that) and cooperative launch */
     if (model == SB_MODEL_QWEN && !(flags & SB_FLAG_MULTI_KERNEL) && c->sms >= 128) {
         e->mk_splits = c->sms / QW_NH;
-        if (e->mk_splits > 16) e->mk_splits = 16; /* the combine handles <= 16 splits per head */
+        if (e->mk_splits > SB_MK_SPLITS_MAX) e->mk_splits = SB_MK_SPLITS_MAX;
         e->mk_score_cap = (CEIL_DIV(max_ctx, e->mk_splits) + 8 + 3) & ~3; /* multiple of 4 floats */
         e->mk_smem = mk_smem_bytes(e->mk_score_cap);
         int coop = 0;
@@ -351,14 +350,16 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     CARVE(counters, groups * 4);
     CARVE(step, sizeof(SbStep));
     CARVE(tokens, (size_t)(max_ctx + 2) * 4);
-    CARVE(bar, 4);
+    CARVE(ll, (size_t)SB_MK_LL_WORDS * 8);
+    CARVE(sync, 8);
     CARVE(err, 4);
 #undef CARVE
     if (cuMemAlloc(&e->scratch, off)) { sb_fail(SB_ERR_STATE, "scratch allocation", __FILE__, __LINE__); goto fail; }
     e->x += e->scratch; e->q += e->scratch; e->att += e->scratch; e->hid += e->scratch;
     e->logits += e->scratch; e->part += e->scratch; e->counters += e->scratch; e->step += e->scratch;
     e->tokens += e->scratch;
-    e->bar += e->scratch;
+    e->ll += e->scratch;
+    e->sync += e->scratch;
     e->err += e->scratch;
     if (cuMemsetD8Async(e->scratch, 0, off, e->stream) || cuMemsetD8Async(e->kv, 0, kv_bytes, e->stream) ||
         cuStreamSynchronize(e->stream)) {
@@ -419,6 +420,17 @@ double sb_engine_step_bytes(sb_engine *e) {
 /* ------------------------------------------------------------------ stepping */
 /* A persistent-kernel barrier that timed out leaves *err set (the kernel
  * returned early instead of hanging); report it and clear the flag. */
+/* Clear the flagged words and the sequence number (epoch 0 never matches). */
+static int mk_clear_words(sb_engine *e) {
+    SB_CK(cuMemsetD8Async(e->ll, 0, (size_t)SB_MK_LL_WORDS * 8, e->stream));
+    SB_CK(cuMemsetD32Async(e->sync, 0, 2, e->stream));
+    e->mk_steps = 0;
+    return 0;
+}
+
+/* A persistent-kernel wait that timed out leaves *err set (the kernel
+ * returned early instead of hanging); report it, and reset the exchange
+ * words so the aborted step's stale words cannot match a later epoch. */
 static int check_device_error(sb_engine *e) {
     if (!e->mk) return 0;
     int err = 0;
@@ -426,13 +438,25 @@ static int check_device_error(sb_engine *e) {
     SB_CK(cuStreamSynchronize(e->stream));
     if (err) {
         SB_CK(cuMemsetD32Async(e->err, 0, 1, e->stream));
+        int rc = mk_clear_words(e);
+        if (rc) return rc;
         SB_CK(cuStreamSynchronize(e->stream));
-        return sb_fail(SB_ERR_STATE, "decode step aborted: a grid barrier wait timed out", __FILE__, __LINE__);
+        return sb_fail(SB_ERR_STATE, "decode step aborted: a wait inside the persistent kernel timed out", __FILE__,
+                       __LINE__);
     }
     return 0;
 }
 
+/* The epoch packs the step sequence number above 7 stage bits into 32 bits:
+ * clear the words well before the sequence number could wrap. */
+static int mk_epoch_guard(sb_engine *e) {
+    if (!e->mk || e->mk_steps < (1L << 24)) return 0;
+    return mk_clear_words(e);
+}
+
 static int put_step(sb_engine *e, const SbStep *st) {
+    int rc = mk_epoch_guard(e);
+    if (rc) return rc;
     SB_CK(cuMemcpyHtoDAsync(e->step, st, sizeof *st, e->stream));
     return 0;
 }
