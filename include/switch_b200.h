@@ -89,6 +89,17 @@ int sb_gemv_h(const uint16_t *W, const float *x, const float *bias, float *y, in
  * sum_k h2f(W[n][k]) h2f(X[b][k]), FP32 accumulate and output (the GEMV
  * sweep's y = W x with x FP16).  K % 8 == 0. */
 int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
+/* The same product for B in 1..256 on the 5th-generation tensor cores
+ * (tcgen05, TMA-fed, FP32 accumulation in tensor memory): the batched-decode
+ * and prefill form of gemv_h.  fp16 subnormals are used as subnormals (the
+ * tensor pipe does not flush them).  K % 8 == 0; W, X 16-byte aligned.
+ * Short matrices are split along K through a library-owned workspace and
+ * summed in split order, so results are deterministic.  No counterpart in
+ * the reference (its prefill is gemv_multi, gpt2_kernels.cu:115-155). */
+int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
+/* Reads and clears the tensor-core kernels' device error flag (nonzero after
+ * a bounded wait gave up); synchronises the context first. */
+int sb_tc_error(int *err);
 
 /* ---- decode-step pieces (Qwen2.5 FP16-weight path, qwen_engine.c:205-269)
  * Exposed for kernel-level parity tests; the engines below fuse them.      */

@@ -11,7 +11,7 @@
 extern "C" {
 #endif
 
-enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_COUNT };
+enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_TC, M_COUNT };
 
 typedef enum {
     F_SGEMM_B200 = 0,
@@ -47,6 +47,8 @@ typedef enum {
     F_QWEN_FINALIZE,
     F_QWEN_MK,
     F_FP16_FLUSH,
+    F_GEMM_HH_TC,
+    F_SPLITK_REDUCE,
     F_COUNT
 } sb_fn_id;
 
@@ -57,6 +59,8 @@ typedef struct sb_ctx {
     CUfunction fn[F_COUNT];
     int smem_set[F_COUNT]; /* dynamic smem limit already raised to this */
     int sms;
+    CUdeviceptr tc_ws; /* split-K workspace of the tensor-core GEMM (grown on demand) */
+    size_t tc_ws_bytes;
 } sb_ctx;
 
 /* error reporting (thread-local message) */

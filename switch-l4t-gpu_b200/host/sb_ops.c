@@ -181,3 +181,69 @@ int sb_attn_decode(const float *q, const float *kc, const float *vc, float *out,
     return sb_launch(c, G == 7 ? F_ATTN_G7 : F_ATTN_G1, (unsigned)NKV, (unsigned)max_splits, 128, 0,
                      (CUstream)stream, args, 0);
 }
+
+/* ------------------------------------------------------------------ tensor-core GEMM */
+static int encode_kmajor_fp16(CUtensorMap *tm, const void *base, int K, int rows, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows}, estr[2] = {1, 1};
+    SB_CK(cuTensorMapEncodeTiled(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)base, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+    return 0;
+}
+
+int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream) {
+    SB_ARG(W && X && Y && K > 0 && N >= 0 && B >= 1 && B <= 256, "bad gemm_hh arguments");
+    SB_ARG(K % 8 == 0 && ALIGNED16(W) && ALIGNED16(X), "gemm_hh needs K % 8 == 0 and 16-byte aligned W, X");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (N == 0) return 0;
+    const int n_pad = CEIL_DIV(B, 16) * 16;
+    CUtensorMap tw, tx;
+    int rc = encode_kmajor_fp16(&tw, W, K, N, 128);
+    if (!rc) rc = encode_kmajor_fp16(&tx, X, K, B, n_pad);
+    if (rc) return rc;
+    /* one CTA per 128-row tile; split K when there are too few tiles to
+     * occupy the SMs */
+    const int tiles = CEIL_DIV(N, 128), nchunks = CEIL_DIV(K, 64);
+    int splits = 1;
+    if (tiles < c->sms) {
+        splits = CEIL_DIV(c->sms, tiles);
+        if (splits > nchunks) splits = nchunks;
+    }
+    CUdeviceptr y = DP(Y), ws = 0;
+    if (splits > 1) {
+        const size_t need = (size_t)splits * B * N * 4;
+        if (c->tc_ws_bytes < need) {
+            if (c->tc_ws) cuMemFree(c->tc_ws);
+            c->tc_ws = 0;
+            c->tc_ws_bytes = 0;
+            SB_CK(cuMemAlloc(&c->tc_ws, need));
+            c->tc_ws_bytes = need;
+        }
+        ws = c->tc_ws;
+    }
+    const unsigned smem = 1024 + 4 * (16384 + n_pad * 128) + 256;
+    void *args[] = {&tw, &tx, &y, &ws, &N, &K, &B, (void *)&n_pad, &splits};
+    rc = sb_launch(c, F_GEMM_HH_TC, (unsigned)(tiles * splits), 1, 192, smem, (CUstream)stream, args, 0);
+    if (rc || splits == 1) return rc;
+    long total = (long)B * N;
+    void *rargs[] = {&ws, &y, &total, &splits};
+    long g = CEIL_DIV(total, 256);
+    if (g > 8L * c->sms) g = 8L * c->sms;
+    return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
+}
+
+int sb_tc_error(int *err) {
+    SB_ARG(err, "null pointer");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr p;
+    size_t bytes;
+    SB_CK(cuCtxSynchronize());
+    SB_CK(cuModuleGetGlobal(&p, &bytes, c->mod[M_TC], "tc_err"));
+    SB_CK(cuMemcpyDtoH(err, p, 4));
+    if (*err) SB_CK(cuMemsetD32(p, 0, 1));
+    return 0;
+}

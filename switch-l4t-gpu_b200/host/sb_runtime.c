@@ -16,6 +16,7 @@ extern const unsigned char sb_img_switch_gpu[], sb_img_switch_gpu_end[];
 extern const unsigned char sb_img_gemv[], sb_img_gemv_end[];
 extern const unsigned char sb_img_gpt2[], sb_img_gpt2_end[];
 extern const unsigned char sb_img_qwen[], sb_img_qwen_end[];
+extern const unsigned char sb_img_tc[], sb_img_tc_end[];
 
 static const struct {
     const char *name;
@@ -25,6 +26,7 @@ static const struct {
     {"gemv", sb_img_gemv, sb_img_gemv_end},
     {"gpt2", sb_img_gpt2, sb_img_gpt2_end},
     {"qwen", sb_img_qwen, sb_img_qwen_end},
+    {"tc", sb_img_tc, sb_img_tc_end},
 };
 
 static const struct {
@@ -64,6 +66,8 @@ static const struct {
     [F_QWEN_FINALIZE] = {M_QWEN, "sb_finalize"},
     [F_QWEN_MK] = {M_QWEN, "qwen_decode_mk"},
     [F_FP16_FLUSH] = {M_QWEN, "fp16_flush_subnormals"},
+    [F_GEMM_HH_TC] = {M_TC, "gemm_hh_tc"},
+    [F_SPLITK_REDUCE] = {M_TC, "gemm_splitk_reduce"},
 };
 
 /* ---------------------------------------------------------------- errors */

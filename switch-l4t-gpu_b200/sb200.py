@@ -17,7 +17,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_DIR = os.path.join(_HERE, "lib")
 BIN_DIR = os.path.join(_HERE, "bin")
 LIB_PATH = os.path.join(LIB_DIR, "libswitch_b200.so")
-CUBINS = {m: os.path.join(LIB_DIR, m + ".cubin") for m in ("switch_gpu", "gemv", "gpt2", "qwen")}
+CUBINS = {m: os.path.join(LIB_DIR, m + ".cubin") for m in ("switch_gpu", "gemv", "gpt2", "qwen", "tc")}
 
 MODEL_QWEN = 1
 MODEL_GPT2 = 2
@@ -81,6 +81,8 @@ def lib():
     _sig(L.sb_gemv_multi_f32, I, P, P, P, P, I, I, I, P)
     _sig(L.sb_gemv_h, I, P, P, P, P, I, I, P)
     _sig(L.sb_gemv_hh, I, P, P, P, I, I, I, P)
+    _sig(L.sb_gemm_hh, I, P, P, P, I, I, I, P)
+    _sig(L.sb_tc_error, I, P)
     _sig(L.sb_rmsnorm, I, P, P, P, I, F, I, P)
     _sig(L.sb_rope, I, P, P, P, I, I, I, I, P)
     _sig(L.sb_swiglu, I, P, P, P, I, P)
@@ -186,6 +188,18 @@ def gemv_h(W, x, bias, y, K, N, stream=None):
 
 def gemv_hh(W, X, Y, K, N, B, stream=None):
     check(lib().sb_gemv_hh(_p(W), _p(X), _p(Y), K, N, B, _s(stream)))
+
+
+def gemm_hh(W, X, Y, K, N, B, stream=None):
+    """Tensor-core (tcgen05) Y[b][n] = sum_k W[n][k] X[b][k], B <= 256."""
+    check(lib().sb_gemm_hh(_p(W), _p(X), _p(Y), K, N, B, _s(stream)))
+
+
+def tc_error():
+    """Read and clear the tensor-core kernels' device error flag."""
+    e = ctypes.c_int()
+    check(lib().sb_tc_error(ctypes.byref(e)))
+    return e.value
 
 
 def rmsnorm(x, w, y, n, eps, rows=1, stream=None):

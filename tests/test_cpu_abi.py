@@ -1,5 +1,5 @@
 """CPU-side checks of the drop-in boundary: the C-ABI library loads, exports
-every function include/switch_b200.h declares, embeds the four module images
+every function include/switch_b200.h declares, embeds the five module images
 (identical to the cubin files the reference hosts would load), and the
 synthetic inputs are deterministic and in the reference layouts."""
 import ctypes
