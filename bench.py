@@ -23,8 +23,8 @@ needed between timed steps.
 Secondary keys of the same line: "sgemm" -- 16384^3 FP32 SGEMM sharded by
 row panels over all ranks (strong scaling) with the NCCL all-gather of C,
 compute-only and with the gather, per-GPU fraction of the live FP32 FMA
-peak; "gemv" -- the standalone FP16 GEMV sweep (batch 1, 4 and 16, the
-last on the tcgen05 tensor cores) in GB/s against the HBM peak.
+peak; "gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4
+and 16 on the tcgen05 tensor cores) in GB/s against the HBM peak.
 
 `--impl reference` times the reference's own CPU decode (cpu_forward of
 gpu-llm/engine/qwen_engine.c compiled unmodified into oracle/_ref) on the
@@ -168,7 +168,7 @@ def ncu_traffic():
     p = os.path.join(REPO, "profiles", "ncu_traffic.json")
     try:
         with open(p) as f:
-            return json.load(f)
+            return {k: v for k, v in json.load(f).items() if not k.startswith("_")}
     except (OSError, ValueError):
         return {}
 
@@ -307,9 +307,9 @@ def sgemm_section(torch, dev, dist_on, steps, warmup):
 
 
 def gemv_section(torch, dev):
-    """Standalone FP16 GEMV sweep y = W.x (fp16 W and x, fp32 y) at batch 1,
-    4 and 16 (the last on the tensor cores); W copies rotated through 1 GiB so
-    every launch streams from HBM."""
+    """Standalone FP16 GEMV sweep y = W.x (fp16 W and x, fp32 y) at batch 1
+    (CUDA cores), 4 and 16 (tcgen05 tensor cores); W copies rotated through
+    1 GiB so every launch streams from HBM."""
     import sb200
     peaks = measured_peaks()
     peak = float(peaks["hbm_gbs"]) if peaks and peaks.get("hbm_gbs") else FALLBACK_HBM_GBS
@@ -322,7 +322,7 @@ def gemv_section(torch, dev):
         for Bw in (1, 4, 16):
             X = torch.randn(Bw, K, device=dev).half()
             Y = torch.empty(Bw, N, device=dev)
-            fn = sb200.gemm_hh if Bw == 16 else sb200.gemv_hh  # batch 16: tcgen05 tensor cores
+            fn = sb200.gemv_hh if Bw == 1 else sb200.gemm_hh  # batches 4 and 16: tcgen05 tensor cores
             for i in range(min(ncopy, 4)):
                 fn(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -339,7 +339,7 @@ def gemv_section(torch, dev):
                                      "l2": "rotating copies" if ncopy * wsz * 2 > 4 * 126e6 else "L2-resident"}
     del pool
     torch.cuda.empty_cache()
-    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1, b4: gemv_hh4 (CUDA cores); b16: gemm_hh_tc (tcgen05)",
+    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1 (CUDA cores); b4, b16: gemm_hh_tc (tcgen05)",
             "peak": peak, "unit": "GB/s", "shapes": out}
 
 
