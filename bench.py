@@ -23,7 +23,7 @@ needed between timed steps.
 Secondary keys of the same line: "sgemm" -- 16384^3 FP32 SGEMM sharded by
 row panels over all ranks (strong scaling) with the NCCL all-gather of C,
 compute-only and with the gather, per-GPU fraction of the live FP32 FMA
-peak; "gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4
+peak; "sgemm_3xtf32" -- the same on the opt-in 3xTF32 tensor-core kernel; "gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4
 and 16 on the tcgen05 tensor cores) in GB/s against the HBM peak.
 
 `--impl reference` times the reference's own CPU decode (cpu_forward of
@@ -254,19 +254,28 @@ def fp32_peak_tflops(torch, dev):
     return flops / (e0.elapsed_time(e1) * 1e-3) / 1e12
 
 
-def sgemm_section(torch, dev, dist_on, steps, warmup):
+def sgemm_section(torch, dev, dist_on, steps, warmup, kernel="fp32"):
     """16384^3 FP32 SGEMM row-panel sharded over all ranks (strong scaling):
-    compute-only and with the NCCL all-gather of C, max over ranks."""
+    compute-only and with the NCCL all-gather of C, max over ranks.
+    kernel "3xtf32" is the opt-in tensor-pipe variant (reported separately)."""
     import sgemm_dist
     n = SGEMM_N
-    ps = sgemm_dist.PanelSgemm(n, n, n)
+    ps = sgemm_dist.PanelSgemm(n, n, n, kernel=kernel)
     gA = torch.Generator(device=dev)
     gA.manual_seed(5000 + RANK)
     gB = torch.Generator(device=dev)
     gB.manual_seed(777)  # B is the same on every rank
     A = torch.rand(ps.rows, n, generator=gA, device=dev) * 2 - 1
     B = torch.rand(n, n, generator=gB, device=dev) * 2 - 1
-    peak = fp32_peak_tflops(torch, dev)
+    if kernel == "fp32":
+        peak, peak_src, bound = fp32_peak_tflops(torch, dev), "fma_peak kernel, this run (of measured)", "fp32"
+    else:
+        mp = measured_peaks()
+        bf16 = float(mp["bf16_tflops"]) if mp and mp.get("bf16_tflops") else 1590.0
+        peak = bf16 / 2 / 3  # dense TF32 = half the bf16 rate; 3 products per useful one
+        peak_src = ("measured bf16 cuBLAS / 2 (TF32) / 3 (products)" if mp and mp.get("bf16_tflops")
+                    else "fallback 1590 bf16 / 2 / 3")
+        bound = "tensor"
     cur = torch.cuda.current_stream(dev)
 
     def step():
@@ -297,9 +306,11 @@ def sgemm_section(torch, dev, dist_on, steps, warmup):
            "compute_ms": round(comp_ms, 3), "allgather_ms": round(tot_ms - comp_ms, 3), "n_gpus": WORLD,
            "scaling": "strong", "steps": steps,
            "parallelism": f"row panels x{WORLD}, B replicated" + (", NCCL all-gather of C" if WORLD > 1 else ""),
-           "kernel": "sgemm_b200 (FP32 FFMA2, 128x128x8 tiles, 2 CTAs/SM)", "dtype": "f32",
-           "roofline": {"bound": "fp32", "achieved": round(per_gpu, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
-                        "frac": round(per_gpu / peak, 4), "peak_source": "fma_peak kernel, this run (of measured)"},
+           "kernel": ("sgemm_b200 (FP32 FFMA2, 128x128x8 tiles, 2 CTAs/SM)" if kernel == "fp32" else
+                      "sgemm_3xtf32_tc (tcgen05 kind::tf32, 3xTF32 split, 128x128x32 tiles, B transposed once)"),
+           "dtype": "f32",
+           "roofline": {"bound": bound, "achieved": round(per_gpu, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                        "frac": round(per_gpu / peak, 4), "peak_source": peak_src},
            "l2": "no flush: 1 GiB operands > 126 MB L2"}
     del A, B, ps
     torch.cuda.empty_cache()
@@ -485,6 +496,7 @@ def run_b200(args):
     eng.close()
     if not args.no_secondary:
         line["sgemm"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3)
+        line["sgemm_3xtf32"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3, kernel="3xtf32")
         line["gemv"] = gemv_section(torch, dev)
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
         try:

@@ -97,6 +97,12 @@ int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
  * summed in split order, so results are deterministic.  No counterpart in
  * the reference (its prefill is gemv_multi, gpt2_kernels.cu:115-155). */
 int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
+/* Opt-in SGEMM on the TF32 tensor pipe with the 3xTF32 split (big/small
+ * parts of each operand, three products accumulated in FP32): the contract
+ * of sb_sgemm (row-major C = A B) at FP32-level accuracy (relative Frobenius
+ * error ~1e-6) and tensor-core speed.  K % 4 == 0, N % 4 == 0, 16-byte
+ * aligned pointers.  No counterpart in the reference. */
+int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
 /* Reads and clears the tensor-core kernels' device error flag (nonzero after
  * a bounded wait gave up); synchronises the context first. */
 int sb_tc_error(int *err);

@@ -224,3 +224,229 @@ extern "C" __global__ void gemm_splitk_reduce(const float *__restrict__ ws, floa
         Y[i] = acc;
     }
 }
+
+// ---------------------------------------------------------------------------
+// sgemm_3xtf32_tc: opt-in FP32 SGEMM C = A.B (row-major, the contract of the
+// reference's sgemm kernels, switch_gpu.cu:5-39) on the TF32 tensor pipe with
+// the 3xTF32 split: each staged operand tile X is rewritten in place as
+// big = X with its 13 low mantissa bits cleared (exact TF32) plus a second
+// tile small = X - big (exact in FP32), and every k-step issues
+// small_A.big_B + big_A.small_B + big_A.big_B into the same FP32 TMEM
+// accumulator.  The dropped small.small term is ~2^-22 relative, so the
+// result is FP32-accurate (relative Frobenius error ~1e-6 against the FP32
+// loop) at tensor-pipe speed.
+//   * B is first transposed (transpose_f32) into a K-major copy Bt[N][K];
+//     reading B's rows directly as an MN-major tf32 operand produced zero
+//     products on this part, so both operands use the K-major descriptor;
+//   * CTA tile 128 x 128, k-slice 32, 3-stage TMA ring (A box {32 k, 128
+//     rows}, Bt box {32 k, 128 rows}), 128-byte swizzle;
+//   * warp 0 lane 0 TMA producer; warps 2-5 split each stage (big/small),
+//     promote finished accumulators into FP32 registers, and store C;
+//     warp 1 lane 0 issues tcgen05.mma kind::tf32 (M=128, N=128, K=8);
+//   * M, N arbitrary (TMA zero-fills outside), K % 4 == 0 (16-byte TMA
+//     strides) and N % 4 == 0 (vector stores).
+namespace t3 {
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, THREADS = 192;
+// The tensor pipe's FP32 accumulation is not IEEE-rounded and its error
+// grows with the length of an accumulation chain (measured: one chain over
+// K = 2048 gave a relative error of 1.5e-5; 4096-long chains at K = 16384
+// gave 2.9e-5).  So every CHUNK k-slices (512 k) the MMAs switch to the
+// other of two TMEM accumulators, and the epilogue warps add the finished one
+// into FP32 registers with IEEE adds ("promotion"), two slices later, so the
+// MMAs never wait for it.
+constexpr int NACC = 2, CHUNK = 16;
+constexpr int TILE = BM * BK * 4;  // 16 KB: the A tile, the Bt tile, and their small parts
+constexpr int STAGE = 4 * TILE;
+SB_DEV uint64_t desc_k(const void *p) {  // K-major, 128-byte rows, 8-row atoms 1024 B apart
+    return ((tck::smem_u32(p) >> 4) & 0x3fffull) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+SB_DEV uint32_t idesc_tf32() {
+    return (1u << 4)                             // D f32
+           | (2u << 7) | (2u << 10)              // A, B tf32, both K-major
+           | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+SB_DEV void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+            d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+SB_DEV void mbar_arrive(uint64_t *mb) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tck::smem_u32(mb)) : "memory");
+}
+}  // namespace t3
+
+// grid: ceil(M/128) * ceil(N/128) CTAs (blockIdx.x = tile_m * tiles_n + tile_n);
+// block t3::THREADS; dynamic smem: 1024 + STAGES * STAGE + 256 bytes.
+extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
+    sgemm_3xtf32_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_bt,
+                    float *__restrict__ C, int M, int N, int K) {
+    using namespace t3;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // stage s: [A | Bt | A small | Bt small], 16 KB each
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE);
+    uint64_t *full = bars, *conv = bars + STAGES, *empty = bars + 2 * STAGES;
+    uint64_t *acc_full = bars + 3 * STAGES, *acc_empty = acc_full + NACC;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + NACC);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + BN - 1) / BN;
+    const int m0 = (blockIdx.x / tiles_n) * BM, n0 = (blockIdx.x % tiles_n) * BN;
+    const int nk = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            tck::mbar_init(&full[s], 1);
+            tck::mbar_init(&conv[s], 128);
+            tck::mbar_init(&empty[s], 1);
+        }
+        for (int q = 0; q < NACC; q++) {
+            tck::mbar_init(&acc_full[q], 1);
+            tck::mbar_init(&acc_empty[q], 128);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tck::smem_u32(tmem_slot)),
+                     "r"(BN * NACC)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            int issued = 0;
+            for (int kt = 0; kt < nk; kt++, issued++) {
+                const int s = kt % STAGES;
+                if (kt >= STAGES && !tck::mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) break;
+                unsigned char *st = smem + (size_t)s * STAGE;
+                tck::mbar_expect_tx(&full[s], 2 * TILE);
+                tck::tma_2d(st, &tm_a, kt * BK, m0, &full[s]);
+                tck::tma_2d(st + TILE, &tm_bt, kt * BK, n0, &full[s]);
+            }
+            for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
+                tck::mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            const uint32_t idesc = idesc_tf32();
+            for (int kt = 0; kt < nk; kt++) {
+                const int s = kt % STAGES, c = kt / CHUNK, q = c % NACC;
+                // a chunk's accumulator is reused once the chunk NACC before it was promoted
+                if (kt % CHUNK == 0 && c >= NACC && !tck::mbar_wait(&acc_empty[q], ((c / NACC) - 1) & 1)) break;
+                if (!tck::mbar_wait(&conv[s], (kt / STAGES) & 1)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                unsigned char *st = smem + (size_t)s * STAGE;
+                const uint64_t a = desc_k(st), b = desc_k(st + TILE), as = desc_k(st + 2 * TILE), bs = desc_k(st + 3 * TILE);
+                const uint32_t d = tmem + (uint32_t)(q * BN);
+#pragma unroll
+                for (int k = 0; k < BK / 8; k++) {
+                    const uint64_t dk = 2ull * k;  // +32 B per K=8 step inside the swizzled 128-byte rows
+                    mma_tf32(d, as + dk, b + dk, idesc, (kt % CHUNK > 0 || k > 0) ? 1u : 0u);
+                    mma_tf32(d, a + dk, bs + dk, idesc, 1u);
+                    mma_tf32(d, a + dk, b + dk, idesc, 1u);
+                }
+                tck::mma_commit(&empty[s]);
+                if (kt % CHUNK == CHUNK - 1 || kt == nk - 1) tck::mma_commit(&acc_full[q]);
+            }
+        }
+    } else {
+        // ---- warps 2-5: split each stage into big/small, promote finished
+        // accumulators into FP32 registers, then store C
+        const int ct = threadIdx.x - 64;  // 0..127
+        const int quarter = warp & 3;      // TMEM lanes 32*quarter.. belong to this warp
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        const int nchunks = (nk + CHUNK - 1) / CHUNK;
+        float sum[BN];
+#pragma unroll
+        for (int j = 0; j < BN; j++) sum[j] = 0.f;
+        bool ok = true;
+        int promoted = 0;
+        auto promote = [&](int c) {  // add chunk c's accumulator into sum, release it
+            const int q = c % NACC;
+            ok = ok && tck::mbar_wait(&acc_full[q], (c / NACC) & 1);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+            for (int col = 0; col < BN; col += 16) {
+                float v[16];
+                tck::tmem_ld16(lane_base + (uint32_t)(q * BN + col), v);
+#pragma unroll
+                for (int j = 0; j < 16; j++) sum[col + j] += v[j];
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            t3::mbar_arrive(&acc_empty[q]);
+        };
+        for (int kt = 0; kt < nk && ok; kt++) {
+            const int s = kt % STAGES;
+            ok = tck::mbar_wait(&full[s], (kt / STAGES) & 1);
+            if (!ok) break;
+            unsigned char *st = smem + (size_t)s * STAGE;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {  // A tile, then Bt tile
+                uint4 *src = reinterpret_cast<uint4 *>(st + half * TILE);
+                uint4 *dst = reinterpret_cast<uint4 *>(st + (2 + half) * TILE);
+#pragma unroll 4
+                for (int i = ct; i < TILE / 16; i += 128) {
+                    uint4 v = src[i], big, small;
+                    big.x = v.x & 0xFFFFE000u; big.y = v.y & 0xFFFFE000u;
+                    big.z = v.z & 0xFFFFE000u; big.w = v.w & 0xFFFFE000u;
+                    small.x = __float_as_uint(__uint_as_float(v.x) - __uint_as_float(big.x));
+                    small.y = __float_as_uint(__uint_as_float(v.y) - __uint_as_float(big.y));
+                    small.z = __float_as_uint(__uint_as_float(v.z) - __uint_as_float(big.z));
+                    small.w = __float_as_uint(__uint_as_float(v.w) - __uint_as_float(big.w));
+                    src[i] = big;
+                    dst[i] = small;
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+            mbar_arrive(&conv[s]);
+            // chunk c is promoted two slices after it ended, when its MMAs have drained
+            if (kt >= CHUNK + 1 && (kt - 1) % CHUNK == 0) promote(promoted++);
+        }
+        while (ok && promoted < nchunks) promote(promoted++);
+        const int row = m0 + quarter * 32 + lane;
+        if (ok && row < M) {
+            float *crow = C + (size_t)row * N + n0;
+            if (n0 + BN <= N) {
+#pragma unroll
+                for (int j = 0; j < BN; j += 4) *reinterpret_cast<float4 *>(crow + j) = make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < BN; j++)
+                    if (n0 + j < N) crow[j] = sum[j];
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(BN * NACC))
+                     : "memory");
+    }
+}
+
+// out[c][r] = in[r][c] for a rows x cols FP32 matrix (32 x 32 tiles through
+// shared memory, both sides coalesced); grid (ceil(cols/32), ceil(rows/32)),
+// block 256 (1-D: tx = thread % 32, ty = thread / 32 in 0..7).
+extern "C" __global__ void __launch_bounds__(256) transpose_f32(const float *__restrict__ in, float *__restrict__ out,
+                                                               int rows, int cols) {
+    __shared__ float t[32][33];
+    if (blockDim.x != 256) return;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = ty; i < 32; i += 8) {
+        const int r = r0 + i, c = c0 + tx;
+        if (r < rows && c < cols) t[i][tx] = in[(size_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int c = c0 + i, r = r0 + tx;
+        if (c < cols && r < rows) out[(size_t)c * rows + r] = t[tx][i];
+    }
+}

@@ -49,6 +49,8 @@ typedef enum {
     F_FP16_FLUSH,
     F_GEMM_HH_TC,
     F_SPLITK_REDUCE,
+    F_SGEMM_3XTF32,
+    F_TRANSPOSE_F32,
     F_COUNT
 } sb_fn_id;
 
@@ -61,6 +63,8 @@ typedef struct sb_ctx {
     int sms;
     CUdeviceptr tc_ws; /* split-K workspace of the tensor-core GEMM (grown on demand) */
     size_t tc_ws_bytes;
+    CUdeviceptr tc_bt; /* K-major copy of B for the 3xTF32 SGEMM (grown on demand) */
+    size_t tc_bt_bytes;
 } sb_ctx;
 
 /* error reporting (thread-local message) */

@@ -235,6 +235,49 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
 }
 
+/* rows x K fp32, K-major, box {32 k, 128 rows}, 128-byte swizzle */
+static int encode_kmajor_f32(CUtensorMap *tm, const void *base, int K, int rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows}, strides[1] = {(cuuint64_t)K * 4};
+    const cuuint32_t box[2] = {32, 128}, estr[2] = {1, 1};
+    SB_CK(cuTensorMapEncodeTiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+    return 0;
+}
+
+int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream) {
+    SB_ARG(A && B && C && M >= 0 && N >= 0 && K > 0, "bad sgemm_3xtf32 arguments");
+    SB_ARG(K % 4 == 0 && N % 4 == 0 && ALIGNED16(A) && ALIGNED16(B) && ALIGNED16(C),
+           "sgemm_3xtf32 needs K % 4 == 0, N % 4 == 0 and 16-byte aligned A, B, C");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (M == 0 || N == 0) return 0;
+    const long tiles = (long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128);
+    SB_ARG(tiles < 0x7fffffffL, "sgemm_3xtf32: too many tiles");
+    /* Bt = B^T (K-major) in a library-owned workspace, grown on demand */
+    const size_t need = (size_t)K * N * 4;
+    if (c->tc_bt_bytes < need) {
+        if (c->tc_bt) cuMemFree(c->tc_bt);
+        c->tc_bt = 0;
+        c->tc_bt_bytes = 0;
+        SB_CK(cuMemAlloc(&c->tc_bt, need));
+        c->tc_bt_bytes = need;
+    }
+    CUdeviceptr bsrc = DP(B), bt = c->tc_bt;
+    void *targs[] = {&bsrc, &bt, &K, &N};
+    int rc = sb_launch(c, F_TRANSPOSE_F32, (unsigned)CEIL_DIV(N, 32), (unsigned)CEIL_DIV(K, 32), 32 * 8, 0,
+                       (CUstream)stream, targs, 0);
+    if (rc) return rc;
+    CUtensorMap ta, tb;
+    rc = encode_kmajor_f32(&ta, A, K, M);
+    if (!rc) rc = encode_kmajor_f32(&tb, (const void *)(uintptr_t)bt, K, N);
+    if (rc) return rc;
+    CUdeviceptr cc = DP(C);
+    void *args[] = {&ta, &tb, &cc, &M, &N, &K};
+    const unsigned smem = 1024 + 3 * 65536 + 256;
+    return sb_launch(c, F_SGEMM_3XTF32, (unsigned)tiles, 1, 192, smem, (CUstream)stream, args, 0);
+}
+
 int sb_tc_error(int *err) {
     SB_ARG(err, "null pointer");
     sb_ctx *c = sb_ctx_get();

@@ -83,6 +83,7 @@ def lib():
     _sig(L.sb_gemv_hh, I, P, P, P, I, I, I, P)
     _sig(L.sb_gemm_hh, I, P, P, P, I, I, I, P)
     _sig(L.sb_tc_error, I, P)
+    _sig(L.sb_sgemm_3xtf32, I, P, P, P, I, I, I, P)
     _sig(L.sb_rmsnorm, I, P, P, P, I, F, I, P)
     _sig(L.sb_rope, I, P, P, P, I, I, I, I, P)
     _sig(L.sb_swiglu, I, P, P, P, I, P)
@@ -193,6 +194,11 @@ def gemv_hh(W, X, Y, K, N, B, stream=None):
 def gemm_hh(W, X, Y, K, N, B, stream=None):
     """Tensor-core (tcgen05) Y[b][n] = sum_k W[n][k] X[b][k], B <= 256."""
     check(lib().sb_gemm_hh(_p(W), _p(X), _p(Y), K, N, B, _s(stream)))
+
+
+def sgemm_3xtf32(A, B, C, M, N, K, stream=None):
+    """Opt-in FP32 SGEMM on the TF32 tensor pipe (3xTF32 split)."""
+    check(lib().sb_sgemm_3xtf32(_p(A), _p(B), _p(C), M, N, K, _s(stream)))
 
 
 def tc_error():

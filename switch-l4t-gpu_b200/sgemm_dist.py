@@ -44,14 +44,24 @@ def _cuda_compute(A_panel, B, C_panel, rows, N, K, stream):
     sb200.sgemm(A_panel, B, C_panel, rows, N, K, stream)
 
 
+def _tf32x3_compute(A_panel, B, C_panel, rows, N, K, stream):
+    import sb200
+    sb200.sgemm_3xtf32(A_panel, B, C_panel, rows, N, K, stream)
+
+
+KERNELS = {"fp32": _cuda_compute, "3xtf32": _tf32x3_compute}
+
+
 class PanelSgemm:
     """Reusable buffers for C = A.B sharded by row panels over `group`.
 
     A_panel: this rank's rows [row0, row1) of A (contiguous, rows x K).
     B:       the whole B (K x N), replicated on every rank.
+    kernel:  "fp32" (CUDA-core FFMA, the default) or "3xtf32" (opt-in, the
+             TF32 tensor pipe with the 3xTF32 split).
     """
 
-    def __init__(self, M, N, K, group=None, device=None, chunks=1, compute=None):
+    def __init__(self, M, N, K, group=None, device=None, chunks=1, compute=None, kernel="fp32"):
         if M <= 0 or N <= 0 or K <= 0 or chunks < 1:
             raise ValueError("PanelSgemm: M, N, K and chunks must be positive")
         self.M, self.N, self.K = M, N, K
@@ -63,7 +73,9 @@ class PanelSgemm:
         self.row0, self.row1 = panel_bounds(M, self.rank, self.world)
         self.rows = self.row1 - self.row0
         self.chunks = max(1, min(chunks, self.R))
-        self.compute = compute or _cuda_compute
+        if kernel not in KERNELS:
+            raise ValueError(f"PanelSgemm: kernel must be one of {sorted(KERNELS)}")
+        self.compute = compute or KERNELS[kernel]
         # gathered C, padded to P*R rows; rows [0, M) are the product
         self.C_pad = torch.empty(self.world * self.R, N, dtype=torch.float32, device=self.device)
         self.C = self.C_pad[:M]
