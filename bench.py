@@ -485,7 +485,8 @@ def run_b200(args):
                        parallelism=f"replicas x{WORLD} (decode does not shard)"),
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": N_PROMPT * 4 + 48,
                 "d2h_bytes_per_step": (N_PROMPT + N_GEN + 1) * 4 + 48,
-                "note": "sb_engine_generate: prompt from pinned host memory, prefill 32 + decode 256, ids back"},
+                "note": "sb_engine_generate: prompt from pinned host memory, batched tensor-core prefill of "
+                        "the first 31 prompt tokens, 257 decode steps, ids back"},
         "gpu_launches": args.steps * N_GEN * eng.launches_per_step(True),
         "step_kernel": "persistent whole-step kernel (1 cooperative launch per token)" if eng.persistent
         else "one kernel per stage (123 launches per token)",

@@ -148,6 +148,8 @@ typedef struct sb_engine sb_engine;
 #define SB_FLAG_NO_PDL 2u    /* no programmatic dependent launch            */
 #define SB_FLAG_MULTI_KERNEL 4u /* Qwen: one kernel per stage instead of the
                                  * persistent whole-step kernel              */
+#define SB_FLAG_NO_PREFILL 8u /* Qwen: sb_engine_generate primes the prompt one
+                               * token per step instead of sb_engine_prefill */
 #define SB_GEN_STOP_EOS 1u   /* stop at the model's end tokens (reference behaviour) */
 
 /* max_ctx: KV-cache positions (<= 8192 Qwen, <= 1024 GPT-2). NULL on error. */
@@ -170,6 +172,12 @@ int sb_engine_generate(sb_engine *e, const int *prompt, int n_prompt, int n_gen,
  * with_logits=0); finish = synchronise and copy ids back. */
 int sb_engine_begin(sb_engine *e, const int *prompt, int n_prompt, int n_gen, unsigned gen_flags);
 int sb_engine_steps(sb_engine *e, int n, int with_logits);
+/* Qwen, right after sb_engine_begin: the first n prompt tokens (n < n_prompt)
+ * run through every layer together -- weight products as batched fp16
+ * tensor-core GEMMs of hi/lo activation rows (sb_gemm_hh), causal attention
+ * per (token, head) -- filling the KV cache; the step position becomes n.
+ * The reference primes the prompt one token at a time (qwen_engine.c:529). */
+int sb_engine_prefill(sb_engine *e, int n);
 int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out);
 void *sb_engine_stream(sb_engine *e);
 /* Device pointer of the logits buffer (V floats) and the vocabulary size. */

@@ -435,3 +435,143 @@ extern "C" __global__ void fp16_flush_subnormals(uint4 *__restrict__ p, long n16
 // Part 3 -- the persistent whole-step kernel
 // =====================================================================
 #include "qwen_mk.cuh"
+
+// ===========================================================================
+// Batched prompt prefill: T prompt tokens at positions pos0..pos0+T-1 run
+// through each layer together, the weight products on the tensor cores
+// (gemm_hh_tc) instead of T separate matvec passes (the reference primes the
+// prompt one token at a time through cpu/gpu_forward, qwen_engine.c:529).
+// Activations enter the fp16 tensor-core GEMM as two rows each:
+// hi = fp16(x) and lo = fp16(x - hi), so W.x = W.hi + W.lo keeps ~22 bits
+// of x; the GEMM output holds the hi products in rows [0, T) and the lo
+// products in rows [T, 2T).  Prompt tokens need no logits, so only the KV
+// cache is the product of a prefill.
+
+SB_DEV void pf_split(float v, unsigned short *hi, unsigned short *lo) {
+    const __half h = __float2half_rn(v);
+    *hi = __half_as_ushort(h);
+    *lo = __half_as_ushort(__float2half_rn(v - __half2float(h)));
+}
+
+// X[t][:] = embedding row of tokens[pos0 + t].  grid T, block 256.
+extern "C" __global__ void qwen_pf_embed(const unsigned short *__restrict__ emb, const int *__restrict__ tokens,
+                                         float *__restrict__ X, int pos0, int C) {
+    const int t = blockIdx.x, tok = tokens[pos0 + t];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) X[(size_t)t * C + i] = h2f_ftz(emb[(size_t)tok * C + i]);
+}
+
+// XH rows t (hi) and T + t (lo) = split(RMSNorm(X[t]) * g).  grid T, block 256.
+extern "C" __global__ void qwen_pf_rms_split(const float *__restrict__ X, const unsigned short *__restrict__ g,
+                                             unsigned short *__restrict__ XH, int T, int C, float eps) {
+    __shared__ float red[32];
+    const int t = blockIdx.x;
+    const float *x = X + (size_t)t * C;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) s = fmaf(x[i], x[i], s);
+    s = block_sum(s, red);
+    const float inv = 1.0f / sqrtf(__fdiv_rn(s, (float)C) + eps);
+    for (int i = threadIdx.x; i < C; i += blockDim.x)
+        pf_split(__fmul_rn(__fmul_rn(x[i], inv), h2f_ftz(g[i])), XH + (size_t)t * C + i, XH + (size_t)(T + t) * C + i);
+}
+
+// XH rows t / T + t = split(X[t]).  grid T, block 256.
+extern "C" __global__ void qwen_pf_split(const float *__restrict__ X, unsigned short *__restrict__ XH, int T, int n) {
+    const int t = blockIdx.x;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        pf_split(X[(size_t)t * n + i], XH + (size_t)t * n + i, XH + (size_t)(T + t) * n + i);
+}
+
+// QKV of token t = Y[t] + Y[T + t] + bias, RoPE (pairs i, i + HD/2) at
+// pos0 + t for the q and k heads; q -> Q[t], k and v -> the cache rows.
+// grid T, block 256.
+extern "C" __global__ void qwen_pf_qkv(const float *__restrict__ Y, const unsigned short *__restrict__ bqkv,
+                                       const float *__restrict__ cosT, const float *__restrict__ sinT,
+                                       float *__restrict__ Q, float *__restrict__ kc, float *__restrict__ vc, int T,
+                                       int pos0, int C, int NH, int NKV, int HD) {
+    const int t = blockIdx.x, pos = pos0 + t;
+    const int KVD = NKV * HD, NQKV = C + 2 * KVD, hd2 = HD / 2;
+    const float *yh = Y + (size_t)t * NQKV, *yl = Y + (size_t)(T + t) * NQKV;
+    for (int p = threadIdx.x; p < NQKV / 2; p += blockDim.x) {
+        const int h = p / hd2, i = p % hd2, r0 = h * HD + i, r1 = r0 + hd2;
+        float y0 = __fadd_rn(__fadd_rn(yh[r0], yl[r0]), h2f_ftz(bqkv[r0]));
+        float y1 = __fadd_rn(__fadd_rn(yh[r1], yl[r1]), h2f_ftz(bqkv[r1]));
+        if (h < NH + NKV) {
+            const float c = cosT[(size_t)pos * hd2 + i], s = sinT[(size_t)pos * hd2 + i];
+            const float o0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, s));
+            const float o1 = __fadd_rn(__fmul_rn(y0, s), __fmul_rn(y1, c));
+            y0 = o0;
+            y1 = o1;
+        }
+        if (h < NH) {
+            Q[(size_t)t * C + r0] = y0;
+            Q[(size_t)t * C + r1] = y1;
+        } else if (h < NH + NKV) {
+            kc[(size_t)pos * KVD + r0 - C] = y0;
+            kc[(size_t)pos * KVD + r1 - C] = y1;
+        } else {
+            vc[(size_t)pos * KVD + r0 - C - KVD] = y0;
+            vc[(size_t)pos * KVD + r1 - C - KVD] = y1;
+        }
+    }
+}
+
+// Causal GQA attention of token t, head h over positions 0..pos0+t, the
+// reference's arithmetic (scores, max-subtracted softmax, mix; FP32).
+// grid (T, NH), block 128, dynamic smem (pos0 + T) * 4 bytes.
+extern "C" __global__ void qwen_pf_attn(const float *__restrict__ Q, const float *__restrict__ kc,
+                                        const float *__restrict__ vc, float *__restrict__ ATT, int pos0, int C, int NH,
+                                        int NKV, int HD, float scale) {
+    extern __shared__ float sc[];
+    __shared__ float red[32];
+    const int t = blockIdx.x, h = blockIdx.y, g = h / (NH / NKV), KVD = NKV * HD;
+    const int n = pos0 + t + 1;
+    const float *q = Q + (size_t)t * C + h * HD;
+    for (int p = threadIdx.x; p < n; p += blockDim.x) {
+        const float *k = kc + (size_t)p * KVD + g * HD;
+        float d = 0.f;
+        for (int j = 0; j < HD; j++) d = fmaf(q[j], k[j], d);
+        sc[p] = d * scale;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {  // the row maximum, by one warp
+        float mm = -1e30f;
+        for (int p = threadIdx.x; p < n; p += 32) mm = fmaxf(mm, sc[p]);
+        mm = warp_max(mm);
+        if (threadIdx.x == 0) red[0] = mm;
+    }
+    __syncthreads();
+    const float mx = red[0];
+    __syncthreads();
+    float l = 0.f;
+    for (int p = threadIdx.x; p < n; p += blockDim.x) {
+        const float e = expf(sc[p] - mx);
+        sc[p] = e;
+        l += e;
+    }
+    l = block_sum(l, red);
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float acc = 0.f;
+        for (int p = 0; p < n; p++) acc = fmaf(sc[p], vc[(size_t)p * KVD + g * HD + d], acc);
+        ATT[(size_t)t * C + h * HD + d] = acc / l;
+    }
+}
+
+// X[t] += Y[t] + Y[T + t] (the residual add of a product).  grid T, block 256.
+extern "C" __global__ void qwen_pf_resid(const float *__restrict__ Y, float *__restrict__ X, int T, int n) {
+    const int t = blockIdx.x;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        X[(size_t)t * n + i] = __fadd_rn(X[(size_t)t * n + i], __fadd_rn(Y[(size_t)t * n + i], Y[(size_t)(T + t) * n + i]));
+}
+
+// hid = silu(gate) * up from the gate|up product Y (rows of 2*FC), split into
+// hi/lo rows of XH for the down projection.  grid T, block 256.
+extern "C" __global__ void qwen_pf_swiglu_split(const float *__restrict__ Y, unsigned short *__restrict__ XH, int T,
+                                                int FC) {
+    const int t = blockIdx.x;
+    const float *yh = Y + (size_t)t * 2 * FC, *yl = Y + (size_t)(T + t) * 2 * FC;
+    for (int i = threadIdx.x; i < FC; i += blockDim.x) {
+        const float gt = __fadd_rn(yh[i], yl[i]), up = __fadd_rn(yh[FC + i], yl[FC + i]);
+        pf_split(__fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), XH + (size_t)t * FC + i,
+                 XH + (size_t)(T + t) * FC + i);
+    }
+}

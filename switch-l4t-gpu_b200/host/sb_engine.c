@@ -52,6 +52,9 @@ struct sb_engine {
     unsigned mk_smem;
     long mk_steps; /* launches since the flagged words were last cleared */
     CUdeviceptr trace;
+    /* batched prompt prefill (Qwen): activations of up to PF_T tokens */
+    CUdeviceptr pf_x, pf_xh, pf_y, pf_q, pf_att;
+    SbStep st_begin; /* the step state sb_engine_begin wrote */
 };
 
 #define MK_THREADS 512
@@ -375,6 +378,9 @@ fail:
 void sb_engine_destroy(sb_engine *e) {
     if (!e) return;
     if (e->stream) cuStreamSynchronize(e->stream);
+    CUdeviceptr pf[] = {e->pf_x, e->pf_xh, e->pf_y, e->pf_q, e->pf_att};
+    for (int i = 0; i < 5; i++)
+        if (pf[i]) cuMemFree(pf[i]);
     for (int i = 0; i < 2; i++)
         if (e->gexec[i]) cuGraphExecDestroy(e->gexec[i]);
     if (e->scratch) cuMemFree(e->scratch);
@@ -498,6 +504,7 @@ int sb_engine_begin(sb_engine *e, const int *prompt, int n_prompt, int n_gen, un
     st.eos1 = e->model == SB_MODEL_QWEN ? QW_IM_END : -1;
     e->n_prompt = n_prompt;
     e->n_end = st.n_end;
+    e->st_begin = st;
     /* graphs are built before the timed phases start */
     int rc = ensure_graph(e, 0);
     if (!rc) rc = ensure_graph(e, 1);
@@ -531,9 +538,81 @@ int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out) {
     return 0;
 }
 
+/* ------------------------------------------------------------------ prefill */
+#define PF_T 128 /* prompt tokens per batch: 2 * PF_T hi/lo rows <= the GEMM's 256 */
+
+int sb_engine_prefill(sb_engine *e, int n) {
+    if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);
+    SB_ARG(e->model == SB_MODEL_QWEN, "batched prefill is implemented for the Qwen engine");
+    SB_ARG(n >= 0 && n < e->n_prompt, "prefill covers prompt tokens before the last one");
+    if (n == 0) return 0;
+    sb_ctx *c = e->c;
+    if (!e->pf_x) {
+        SB_CK(cuMemAlloc(&e->pf_x, (size_t)PF_T * QW_C * 4));
+        SB_CK(cuMemAlloc(&e->pf_xh, (size_t)2 * PF_T * QW_FC * 2));
+        SB_CK(cuMemAlloc(&e->pf_y, (size_t)2 * PF_T * 2 * QW_FC * 4));
+        SB_CK(cuMemAlloc(&e->pf_q, (size_t)PF_T * QW_C * 4));
+        SB_CK(cuMemAlloc(&e->pf_att, (size_t)PF_T * QW_C * 4));
+    }
+    CUstream s = e->stream;
+    int C = QW_C, FC = QW_FC, NH = QW_NH, NKV = QW_NKV, HD = QW_HD;
+    float eps = 1e-6f, scale = 0.125f;
+    const CUdeviceptr cosT = e->w + QW_OFF_COS, sinT = e->w + QW_OFF_SIN;
+    const uint16_t *xh = (const uint16_t *)(uintptr_t)e->pf_xh;
+    float *y = (float *)(uintptr_t)e->pf_y;
+    for (int p0 = 0; p0 < n; p0 += PF_T) {
+        int T = n - p0 < PF_T ? n - p0 : PF_T;
+        void *ea[] = {&e->w, &e->tokens, &e->pf_x, &p0, &C};
+        int rc = sb_launch(c, F_PF_EMBED, (unsigned)T, 1, 256, 0, s, ea, 0);
+        for (int l = 0; !rc && l < QW_NL; l++) {
+            const CUdeviceptr L = e->w + QW_LBASE + (size_t)l * QW_LSTRIDE;
+            CUdeviceptr g_in = L, wqkv = L + QW_C * 2, bqkv = wqkv + (size_t)QW_QKV * QW_C * 2;
+            CUdeviceptr wo = bqkv + QW_QKV * 2, g_post = wo + (size_t)QW_C * QW_C * 2, wgu = g_post + QW_C * 2;
+            CUdeviceptr wdown = wgu + (size_t)2 * QW_FC * QW_C * 2;
+            CUdeviceptr kc = e->kv + (size_t)l * e->ctx_cap * QW_KVD * 4;
+            CUdeviceptr vc = e->kv + (size_t)(QW_NL + l) * e->ctx_cap * QW_KVD * 4;
+            int twoT = 2 * T;
+            /* QKV of every token (RoPE, KV-cache rows) */
+            void *ra[] = {&e->pf_x, &g_in, &e->pf_xh, &T, &C, &eps};
+            rc = sb_launch(c, F_PF_RMS_SPLIT, (unsigned)T, 1, 256, 0, s, ra, 0);
+            if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wqkv, xh, y, C, QW_QKV, twoT, s);
+            void *qa[] = {&e->pf_y, &bqkv, (void *)&cosT, (void *)&sinT, &e->pf_q, &kc, &vc, &T, &p0, &C, &NH, &NKV, &HD};
+            if (!rc) rc = sb_launch(c, F_PF_QKV, (unsigned)T, 1, 256, 0, s, qa, 0);
+            if (l == QW_NL - 1) break; /* the last layer's output feeds only logits */
+            /* causal attention, O projection + residual */
+            void *aa[] = {&e->pf_q, &kc, &vc, &e->pf_att, &p0, &C, &NH, &NKV, &HD, &scale};
+            if (!rc) rc = sb_launch(c, F_PF_ATTN, (unsigned)T, (unsigned)NH, 128, (unsigned)(p0 + T) * 4, s, aa, 0);
+            void *sa[] = {&e->pf_att, &e->pf_xh, &T, &C};
+            if (!rc) rc = sb_launch(c, F_PF_SPLIT, (unsigned)T, 1, 256, 0, s, sa, 0);
+            if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wo, xh, y, C, QW_C, twoT, s);
+            void *xa[] = {&e->pf_y, &e->pf_x, &T, &C};
+            if (!rc) rc = sb_launch(c, F_PF_RESID, (unsigned)T, 1, 256, 0, s, xa, 0);
+            /* MLP: RMSNorm -> gate|up -> SwiGLU -> down + residual */
+            void *pa[] = {&e->pf_x, &g_post, &e->pf_xh, &T, &C, &eps};
+            if (!rc) rc = sb_launch(c, F_PF_RMS_SPLIT, (unsigned)T, 1, 256, 0, s, pa, 0);
+            if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wgu, xh, y, C, 2 * QW_FC, twoT, s);
+            void *wa[] = {&e->pf_y, &e->pf_xh, &T, &FC};
+            if (!rc) rc = sb_launch(c, F_PF_SWIGLU_SPLIT, (unsigned)T, 1, 256, 0, s, wa, 0);
+            if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wdown, xh, y, FC, QW_C, twoT, s);
+            if (!rc) rc = sb_launch(c, F_PF_RESID, (unsigned)T, 1, 256, 0, s, xa, 0);
+        }
+        if (rc) return rc;
+    }
+    /* the decode steps continue at position n */
+    SbStep st = e->st_begin;
+    st.pos = n;
+    return put_step(e, &st);
+}
+
 int sb_engine_generate(sb_engine *e, const int *prompt, int n_prompt, int n_gen, int *out_ids, int *n_out,
                        unsigned gen_flags) {
     int rc = sb_engine_begin(e, prompt, n_prompt, n_gen, gen_flags);
+    if (!rc && e->model == SB_MODEL_QWEN && !(e->flags & SB_FLAG_NO_PREFILL) && n_prompt > 1) {
+        rc = sb_engine_prefill(e, n_prompt - 1); /* prompt tokens batched on the tensor cores */
+        if (!rc) rc = sb_engine_steps(e, n_gen + 1, 1); /* last prompt token + n_gen */
+        if (!rc) rc = sb_engine_finish(e, out_ids, n_out);
+        return rc;
+    }
     if (!rc) rc = sb_engine_steps(e, n_prompt - 1, 0); /* prompt tokens: no LM head */
     if (!rc) rc = sb_engine_steps(e, n_gen + 1, 1);    /* last prompt token + n_gen */
     if (!rc) rc = sb_engine_finish(e, out_ids, n_out);

@@ -51,6 +51,13 @@ typedef enum {
     F_SPLITK_REDUCE,
     F_SGEMM_3XTF32,
     F_TRANSPOSE_F32,
+    F_PF_EMBED,
+    F_PF_RMS_SPLIT,
+    F_PF_SPLIT,
+    F_PF_QKV,
+    F_PF_ATTN,
+    F_PF_RESID,
+    F_PF_SWIGLU_SPLIT,
     F_COUNT
 } sb_fn_id;
 

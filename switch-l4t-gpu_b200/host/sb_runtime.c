@@ -70,6 +70,13 @@ static const struct {
     [F_SPLITK_REDUCE] = {M_TC, "gemm_splitk_reduce"},
     [F_SGEMM_3XTF32] = {M_TC, "sgemm_3xtf32_tc"},
     [F_TRANSPOSE_F32] = {M_TC, "transpose_f32"},
+    [F_PF_EMBED] = {M_QWEN, "qwen_pf_embed"},
+    [F_PF_RMS_SPLIT] = {M_QWEN, "qwen_pf_rms_split"},
+    [F_PF_SPLIT] = {M_QWEN, "qwen_pf_split"},
+    [F_PF_QKV] = {M_QWEN, "qwen_pf_qkv"},
+    [F_PF_ATTN] = {M_QWEN, "qwen_pf_attn"},
+    [F_PF_RESID] = {M_QWEN, "qwen_pf_resid"},
+    [F_PF_SWIGLU_SPLIT] = {M_QWEN, "qwen_pf_swiglu_split"},
 };
 
 /* ---------------------------------------------------------------- errors */

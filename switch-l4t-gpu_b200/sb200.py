@@ -24,6 +24,7 @@ MODEL_GPT2 = 2
 FLAG_NO_GRAPH = 1
 FLAG_NO_PDL = 2
 FLAG_MULTI_KERNEL = 4
+FLAG_NO_PREFILL = 8
 GEN_STOP_EOS = 1
 
 QWEN = dict(V=151936, C=896, NL=24, NH=14, NKV=2, HD=64, FC=4864, CTX_FILE=8192,
@@ -98,6 +99,7 @@ def lib():
     _sig(L.sb_engine_generate, I, P, P, I, I, P, ctypes.POINTER(I), ctypes.c_uint)
     _sig(L.sb_engine_begin, I, P, P, I, I, ctypes.c_uint)
     _sig(L.sb_engine_steps, I, P, I, I)
+    _sig(L.sb_engine_prefill, I, P, I)
     _sig(L.sb_engine_finish, I, P, P, ctypes.POINTER(I))
     _sig(L.sb_engine_stream, P, P)
     _sig(L.sb_engine_logits, I, P, ctypes.POINTER(P), ctypes.POINTER(I))
@@ -313,6 +315,10 @@ class Engine:
     def begin(self, prompt, n_gen, stop_eos=False):
         arr = (ctypes.c_int * len(prompt))(*prompt)
         check(lib().sb_engine_begin(self.h, arr, len(prompt), n_gen, GEN_STOP_EOS if stop_eos else 0))
+
+    def prefill(self, n):
+        """Qwen: batched prefill of the first n prompt tokens (after begin)."""
+        check(lib().sb_engine_prefill(self.h, n))
 
     def steps(self, n, with_logits):
         check(lib().sb_engine_steps(self.h, n, 1 if with_logits else 0))

@@ -117,3 +117,37 @@ def test_engine_rejects_bad_input(cuda_dev, gpt2_weights, tmp_path):
     bad.write_bytes(b"\0" * 1024)
     with pytest.raises(sb200.SbError):
         sb200.Engine(sb200.MODEL_GPT2, bad, 16)
+
+
+def test_qwen_prefill_matches_stepwise_priming(cuda_dev, qwen_weights):
+    """Batched tensor-core prefill of the prompt vs priming it one step per
+    token: the first generated step's logits agree (2e-3) and both match the
+    oracle; a 150-token prompt exercises two prefill batches (128 + 21)."""
+    for n_prompt in (12, 150):
+        prompt = sb200.synth_ids(n_prompt, sb200.QWEN["V"], 40 + n_prompt)
+        eng = sb200.Engine(sb200.MODEL_QWEN, qwen_weights, 256)
+        ref = orc.Model("qwen", qwen_weights, 256, sb200.QWEN["V"])
+        try:
+            outs = []
+            for mode in ("prefill", "steps"):
+                eng.begin(prompt, 4)
+                if mode == "prefill":
+                    eng.prefill(n_prompt - 1)
+                else:
+                    eng.steps(n_prompt - 1, False)
+                got = np.zeros(sb200.QWEN["V"], dtype=np.float32)
+                eng.forward(prompt[-1], n_prompt - 1, True, got)  # the last prompt token, with logits
+                outs.append(got)
+            for p, t in enumerate(prompt):
+                want = ref.forward(t, p, p == n_prompt - 1)
+            assert _rel(outs[0], outs[1]) <= LOGIT_TOL
+            assert _rel(outs[0], want) <= LOGIT_TOL, f"prefill vs oracle {_rel(outs[0], want):.2e}"
+            assert int(np.argmax(outs[0])) == int(np.argmax(want))
+        finally:
+            eng.close()
+            ref.close()
+
+
+def test_qwen_greedy_stepwise_priming(cuda_dev, qwen_weights):
+    """The greedy check with the one-token-per-step prompt path."""
+    _greedy(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 32, 63, 33, sb200.FLAG_NO_PREFILL)
