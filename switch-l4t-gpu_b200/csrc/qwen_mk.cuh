@@ -247,7 +247,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     float *opart = red + 32;                          // WARPS x HD per-warp partial P.V
     float *ksum = opart + WARPS * HD;                 // WARPS floats: split-K partials / per-warp softmax sums
     float *mlv = ksum + WARPS;                        // NH*SPLITS_MAX (m, l) pairs of the partials
-    __shared__ float wmax_s[WARPS], xown[8];
+    __shared__ float wmax_s[WARPS], xown[8], gu_s[96];
     __shared__ unsigned long long best_s;
     __shared__ __align__(8) uint64_t mbar[WARPS][2 + LM_NB];
 
@@ -351,18 +351,20 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         issue_begin(1, r < or1 ? C : 0);
         if (r < or1) bulk_g2s(wreg + WHEAD, layer_ptr(l) + L_OW + (long)r * C + half * (C / 2), C, &mb[1]);
     };
-    // gate/up pairs gp0 + warp + 16k, k < 3, rows (gate_k, up_k): the byte
-    // count of all pairs is announced with the first piece, then one pair is
-    // issued per stage (S1, S2, S3) to spread the traffic
+    // gate/up rows: the CTA's 2*(gp1-gp0) rows r (pair r/2; gate when r is
+    // even, up when odd) go to warp r % 16, slot row r / 16 -- at most 5 rows
+    // a warp (a pair-per-warp split left one warp with 6 rows when the CTA
+    // owns 33 pairs).  The byte count is announced with the first piece, then
+    // two slot rows are issued per stage (S1, S2, S3) to spread the traffic.
+    const int gu_rows = 2 * (gp1 - gp0);
+    const int gu_nr = max(0, (gu_rows - warp + WARPS - 1) / WARPS);  // this warp's rows (<= 5)
     auto copy_s4_piece = [&](int l, int k) {
         if (lane != 0) return;
-        const int npair = min(3, max(0, (gp1 - (gp0 + warp) + WARPS - 1) / WARPS));
-        if (k == 0) issue_begin(0, (unsigned)npair * 2 * C * 2);
-        if (k < npair) {
-            const unsigned short *W = layer_ptr(l) + L_GATEUP;
-            const int i = gp0 + warp + WARPS * k;
-            bulk_g2s(wreg + (2 * k) * C * 2, W + (long)i * C, C * 2, &mb[0]);
-            bulk_g2s(wreg + (2 * k + 1) * C * 2, W + (long)(FC + i) * C, C * 2, &mb[0]);
+        if (k == 0) issue_begin(0, (unsigned)gu_nr * C * 2);
+        const unsigned short *W = layer_ptr(l) + L_GATEUP;
+        for (int t = 2 * k; t < min(gu_nr, 2 * k + 2); t++) {
+            const int r = warp + WARPS * t;
+            bulk_g2s(wreg + t * C * 2, W + (long)((r & 1) * FC + gp0 + (r >> 1)) * C, C * 2, &mb[0]);
         }
     };
     auto copy_s5 = [&](int l) {  // down rows: warp w -> row or0 + w/2, half w%2 of K
@@ -671,16 +673,17 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         wait_slot(0);
         __syncwarp();
         {
-            // this warp's pairs: gp0 + warp + 16k, k < 3; rows stored (gate_k, up_k)
-            const int npair = min(3, max(0, (gp1 - (gp0 + warp) + WARPS - 1) / WARPS));
-            float a[6];
-            smem_rows_dot<6>(wreg4, CPR, 2 * npair, xlo, xhi, 0, CPR, 0, a);
-            const unsigned e = epoch(l, 3);
+            float a[5];
+            smem_rows_dot<5>(wreg4, CPR, gu_nr, xlo, xhi, 0, CPR, 0, a);
 #pragma unroll
-            for (int k = 0; k < 3; k++) {
-                const float ag = warp_sum(a[2 * k]), au = warp_sum(a[2 * k + 1]);
-                if (k < npair && lane == 0)
-                    ll_put(llhid + gp0 + warp + WARPS * k, __fmul_rn(__fdiv_rn(ag, __fadd_rn(1.0f, expf(-ag))), au), e);
+            for (int t = 0; t < 5; t++) {
+                const float d = warp_sum(a[t]);
+                if (t < gu_nr && lane == 0) gu_s[warp + WARPS * t] = d;
+            }
+            __syncthreads();
+            if (tid < gp1 - gp0) {  // SwiGLU of pair tid: gate row 2 tid, up row 2 tid + 1
+                const float ag = gu_s[2 * tid], au = gu_s[2 * tid + 1];
+                ll_put(llhid + gp0 + tid, __fmul_rn(__fdiv_rn(ag, __fadd_rn(1.0f, expf(-ag))), au), epoch(l, 3));
             }
         }
         stamp(l, 3, 1);
