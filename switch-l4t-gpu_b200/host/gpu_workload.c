@@ -2,7 +2,7 @@
  * reference harness's CLI and JSON contract (gpu_workload.c of
  * pkia/switch-l4t-gpu; consumed by deploy/cluster/gpu_task_example.py).
  *
- *   gpu_workload [--json] [--sizes 256,512,1024] [--membw-mib 2048] [module]
+ *   gpu_workload [--json] [--sizes 256,512,1024] [--membw-mib 2048] [--tf32x3] [module]
  *
  * `module` is a cubin/PTX image loaded with cuModuleLoadData (default: the
  * switch_gpu.cubin installed next to this binary).  Kernels are resolved by
@@ -19,7 +19,8 @@
  *
  * JSON keys are the reference's (ptx, kernels, sgemm, sgemm4, sgemm_opt,
  * membw_gbps, done) plus additive ones (device, sm_count, sgemm_b200,
- * membw_bytes, fp32_peak_gflops_at_max_clock). */
+ * membw_bytes, fp32_peak_gflops_at_max_clock, and with --tf32x3 the opt-in
+ * tensor-core SGEMM of this package: kernels.sgemm_3xtf32, sgemm_3xtf32). */
 #define _GNU_SOURCE
 #include <cuda.h>
 #include <stdint.h>
@@ -28,6 +29,8 @@
 #include <string.h>
 #include <time.h>
 #include <unistd.h>
+
+#include "../../include/switch_b200.h"
 
 static int json_mode;
 #define OUT(...) do { if (!json_mode) printf(__VA_ARGS__); } while (0)
@@ -98,12 +101,16 @@ int main(int argc, char **argv) {
     const char *mod_path = NULL;
     int sizes[16] = {256, 512, 1024}, nsizes = 3;
     long membw_mib = 2048;
+    int tf32x3 = 0;
+    const char *v_t3 = NULL;
+    double t3_ms[16] = {0}, t3_gf[16] = {0};
     for (int i = 1; i < argc; i++) {
         if (!strcmp(argv[i], "--json")) json_mode = 1;
         else if (!strcmp(argv[i], "--sizes") && i + 1 < argc) {
             nsizes = 0;
             for (char *t = strtok(argv[++i], ","); t && nsizes < 16; t = strtok(NULL, ",")) sizes[nsizes++] = atoi(t);
         } else if (!strcmp(argv[i], "--membw-mib") && i + 1 < argc) membw_mib = atol(argv[++i]);
+        else if (!strcmp(argv[i], "--tf32x3")) tf32x3 = 1;
         else mod_path = argv[i];
     }
     if (!mod_path) mod_path = default_module();
@@ -193,6 +200,28 @@ int main(int argc, char **argv) {
             k->gf[si] = 2.0 * n * (double)n * n / (k->ms[si] * 1e-3) / 1e9;
             OUT("%s %dx%dx%d: %.3f ms/iter, %.1f GFLOPS\n", ki == 0 ? "sgemm" : k->name, n, n, n, k->ms[si], k->gf[si]);
         }
+        if (tf32x3) { /* opt-in: sb_sgemm_3xtf32 through the C-ABI library */
+            const float *pa = (const float *)(uintptr_t)dA, *pb = (const float *)(uintptr_t)dB;
+            float *pc = (float *)(uintptr_t)dC;
+            CHK(cuMemsetD32(dC, 0, (size_t)n * n));
+            if (sb_sgemm_3xtf32(pa, pb, pc, n, n, n, NULL)) { fprintf(stderr, "%s\n", sb_last_error()); exit(1); }
+            CHK(cuCtxSynchronize());
+            if (n == 256) {
+                CHK(cuMemcpyDtoH(C, dC, bytes));
+                v_t3 = verify(A, B, C, n, 0) ? "WRONG" : "CORRECT";
+                OUT("sgemm_3xtf32 %d: %s\n", n, v_t3);
+            }
+            CHK(cuEventRecord(e0, NULL));
+            for (int r = 0; r < 10; r++)
+                if (sb_sgemm_3xtf32(pa, pb, pc, n, n, n, NULL)) { fprintf(stderr, "%s\n", sb_last_error()); exit(1); }
+            CHK(cuEventRecord(e1, NULL));
+            CHK(cuEventSynchronize(e1));
+            float ms10 = 0;
+            CHK(cuEventElapsedTime(&ms10, e0, e1));
+            t3_ms[si] = ms10 / 10.0;
+            t3_gf[si] = 2.0 * n * (double)n * n / (t3_ms[si] * 1e-3) / 1e9;
+            OUT("sgemm_3xtf32 %dx%dx%d: %.3f ms/iter, %.1f GFLOPS\n", n, n, n, t3_ms[si], t3_gf[si]);
+        }
         cuMemFree(dA);
         cuMemFree(dB);
         cuMemFree(dC);
@@ -240,12 +269,19 @@ int main(int argc, char **argv) {
         if (ks[1].verdict) printf(",\"sgemm_tiled4\":\"%s\"", ks[1].verdict);
         if (ks[2].verdict) printf(",\"sgemm_opt\":\"%s\"", ks[2].verdict);
         if (ks[3].verdict) printf(",\"sgemm_b200\":\"%s\"", ks[3].verdict);
+        if (v_t3) printf(",\"sgemm_3xtf32\":\"%s\"", v_t3);
         printf("}");
         for (int ki = 0; ki < 4; ki++) {
             if (!ks[ki].f) continue;
             printf(",\"%s\":[", ks[ki].json_key);
             for (int i = 0; i < nsizes; i++)
                 printf("%s{\"n\":%d,\"ms\":%.3f,\"gflops\":%.1f}", i ? "," : "", sizes[i], ks[ki].ms[i], ks[ki].gf[i]);
+            printf("]");
+        }
+        if (tf32x3) {
+            printf(",\"sgemm_3xtf32\":[");
+            for (int i = 0; i < nsizes; i++)
+                printf("%s{\"n\":%d,\"ms\":%.3f,\"gflops\":%.1f}", i ? "," : "", sizes[i], t3_ms[i], t3_gf[i]);
             printf("]");
         }
         printf(",\"membw_gbps\":%.1f,\"membw_bytes\":%.0f,\"device\":\"%s\",\"sm_count\":%d,"
