@@ -103,6 +103,10 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
  * error ~1e-6) and tensor-core speed.  K % 4 == 0, N % 4 == 0, 16-byte
  * aligned pointers.  No counterpart in the reference. */
 int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
+/* The same product with the second operand given transposed: C = A Bt^T for
+ * Bt [N][K] row-major (an [out][in] weight matrix), no transpose pass.  Same
+ * alignment rules.  No counterpart in the reference. */
+int sb_sgemm_nt_3xtf32(const float *A, const float *Bt, float *C, int M, int N, int K, void *stream);
 /* Reads and clears the tensor-core kernels' device error flag (nonzero after
  * a bounded wait gave up); synchronises the context first. */
 int sb_tc_error(int *err);
@@ -148,8 +152,8 @@ typedef struct sb_engine sb_engine;
 #define SB_FLAG_NO_PDL 2u    /* no programmatic dependent launch            */
 #define SB_FLAG_MULTI_KERNEL 4u /* Qwen: one kernel per stage instead of the
                                  * persistent whole-step kernel              */
-#define SB_FLAG_NO_PREFILL 8u /* Qwen: sb_engine_generate primes the prompt one
-                               * token per step instead of sb_engine_prefill */
+#define SB_FLAG_NO_PREFILL 8u /* sb_engine_generate primes the prompt one token
+                               * per step instead of sb_engine_prefill        */
 #define SB_GEN_STOP_EOS 1u   /* stop at the model's end tokens (reference behaviour) */
 
 /* max_ctx: KV-cache positions (<= 8192 Qwen, <= 1024 GPT-2). NULL on error. */
@@ -172,11 +176,14 @@ int sb_engine_generate(sb_engine *e, const int *prompt, int n_prompt, int n_gen,
  * with_logits=0); finish = synchronise and copy ids back. */
 int sb_engine_begin(sb_engine *e, const int *prompt, int n_prompt, int n_gen, unsigned gen_flags);
 int sb_engine_steps(sb_engine *e, int n, int with_logits);
-/* Qwen, right after sb_engine_begin: the first n prompt tokens (n < n_prompt)
- * run through every layer together -- weight products as batched fp16
- * tensor-core GEMMs of hi/lo activation rows (sb_gemm_hh), causal attention
- * per (token, head) -- filling the KV cache; the step position becomes n.
- * The reference primes the prompt one token at a time (qwen_engine.c:529). */
+/* Right after sb_engine_begin: the first n prompt tokens (n < n_prompt) run
+ * through every layer together, filling the KV cache; the step position
+ * becomes n.  Weight products are tensor-core GEMMs -- Qwen: fp16 GEMMs of
+ * hi/lo fp16 activation rows (sb_gemm_hh); GPT-2: 3xTF32 GEMMs against the
+ * FP32 weights (sb_sgemm_nt_3xtf32) -- and attention is causal per (token,
+ * head).  The reference primes Qwen prompts one token at a time
+ * (qwen_engine.c:529) and batches GPT-2's through gemv_multi (gpu_prefill,
+ * gpt2_engine.c:269-326). */
 int sb_engine_prefill(sb_engine *e, int n);
 int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out);
 void *sb_engine_stream(sb_engine *e);

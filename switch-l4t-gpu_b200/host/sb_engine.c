@@ -52,8 +52,8 @@ struct sb_engine {
     unsigned mk_smem;
     long mk_steps; /* launches since the flagged words were last cleared */
     CUdeviceptr trace;
-    /* batched prompt prefill (Qwen): activations of up to PF_T tokens */
-    CUdeviceptr pf_x, pf_xh, pf_y, pf_q, pf_att;
+    /* batched prompt prefill: activations of up to PF_T tokens */
+    CUdeviceptr pf_x, pf_xh, pf_y, pf_q, pf_att, pf_a;
     SbStep st_begin; /* the step state sb_engine_begin wrote */
 };
 
@@ -378,8 +378,8 @@ fail:
 void sb_engine_destroy(sb_engine *e) {
     if (!e) return;
     if (e->stream) cuStreamSynchronize(e->stream);
-    CUdeviceptr pf[] = {e->pf_x, e->pf_xh, e->pf_y, e->pf_q, e->pf_att};
-    for (int i = 0; i < 5; i++)
+    CUdeviceptr pf[] = {e->pf_x, e->pf_xh, e->pf_y, e->pf_q, e->pf_att, e->pf_a};
+    for (int i = 0; i < 6; i++)
         if (pf[i]) cuMemFree(pf[i]);
     for (int i = 0; i < 2; i++)
         if (e->gexec[i]) cuGraphExecDestroy(e->gexec[i]);
@@ -541,11 +541,68 @@ int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out) {
 /* ------------------------------------------------------------------ prefill */
 #define PF_T 128 /* prompt tokens per batch: 2 * PF_T hi/lo rows <= the GEMM's 256 */
 
+/* GPT-2: LayerNorm rows -> 3xTF32 tensor-core products against the [out][in]
+ * weights (FP32 accuracy) -> bias / GELU / residual kernels; causal attention
+ * per (token, head) with the Qwen prefill kernel (12 KV heads = MHA). */
+static int prefill_gpt2(sb_engine *e, int n) {
+    sb_ctx *c = e->c;
+    if (!e->pf_x) {
+        SB_CK(cuMemAlloc(&e->pf_x, (size_t)PF_T * G2_C * 4));
+        SB_CK(cuMemAlloc(&e->pf_a, (size_t)PF_T * G2_FC * 4));
+        SB_CK(cuMemAlloc(&e->pf_y, (size_t)PF_T * G2_FC * 4));
+        SB_CK(cuMemAlloc(&e->pf_q, (size_t)PF_T * G2_C * 4));
+        SB_CK(cuMemAlloc(&e->pf_att, (size_t)PF_T * G2_C * 4));
+    }
+    CUstream s = e->stream;
+    int C = G2_C, FC = G2_FC, NH = G2_NH, HD = G2_HD;
+    float eps = 1e-5f, scale = 0.125f;
+    const CUdeviceptr wte = e->w, wpe = e->w + G2_OFF_WPE * 4;
+    const float *pa = (const float *)(uintptr_t)e->pf_a, *patt = (const float *)(uintptr_t)e->pf_att;
+    float *py = (float *)(uintptr_t)e->pf_y;
+    for (int p0 = 0; p0 < n; p0 += PF_T) {
+        int T = n - p0 < PF_T ? n - p0 : PF_T;
+        void *ea[] = {(void *)&wte, (void *)&wpe, &e->tokens, &e->pf_x, &p0, &C};
+        int rc = sb_launch(c, F_G2PF_EMBED, (unsigned)T, 1, 256, 0, s, ea, 0);
+        for (int l = 0; !rc && l < G2_NL; l++) {
+            const CUdeviceptr lb = e->w + (G2_LBASE + (size_t)l * G2_LAYER) * 4;
+            CUdeviceptr ln1w = lb + G2L_LN1W * 4, ln1b = lb + G2L_LN1B * 4, wqkv = lb + G2L_QKVW * 4;
+            CUdeviceptr bqkv = lb + G2L_QKVB * 4, wo = lb + G2L_AOW * 4, bo = lb + G2L_AOB * 4;
+            CUdeviceptr ln2w = lb + G2L_LN2W * 4, ln2b = lb + G2L_LN2B * 4, wfc = lb + G2L_FCW * 4;
+            CUdeviceptr bfc = lb + G2L_FCB * 4, wp = lb + G2L_PROJW * 4, bp = lb + G2L_PROJB * 4;
+            CUdeviceptr kc = e->kv + (size_t)l * e->ctx_cap * C * 4;
+            CUdeviceptr vc = e->kv + (size_t)(G2_NL + l) * e->ctx_cap * C * 4;
+            void *la[] = {&e->pf_x, &ln1w, &ln1b, &e->pf_a, &C, &eps};
+            rc = sb_launch(c, F_G2_LAYERNORM_ROWS, (unsigned)T, 1, 256, 0, s, la, 0);
+            if (!rc) rc = sb_sgemm_nt_3xtf32(pa, (const float *)(uintptr_t)wqkv, py, T, 3 * C, C, s);
+            void *qa[] = {&e->pf_y, &bqkv, &e->pf_q, &kc, &vc, &p0, &C};
+            if (!rc) rc = sb_launch(c, F_G2PF_QKV, (unsigned)T, 1, 256, 0, s, qa, 0);
+            if (l == G2_NL - 1) break; /* the last layer's output feeds only logits */
+            void *aa[] = {&e->pf_q, &kc, &vc, &e->pf_att, &p0, &C, &NH, &NH, &HD, &scale};
+            if (!rc) rc = sb_launch(c, F_PF_ATTN, (unsigned)T, (unsigned)NH, 128, (unsigned)(p0 + T) * 4, s, aa, 0);
+            if (!rc) rc = sb_sgemm_nt_3xtf32(patt, (const float *)(uintptr_t)wo, py, T, C, C, s);
+            void *ra[] = {&e->pf_y, &bo, &e->pf_x, &C};
+            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_RESID, (unsigned)T, 1, 256, 0, s, ra, 0);
+            void *l2[] = {&e->pf_x, &ln2w, &ln2b, &e->pf_a, &C, &eps};
+            if (!rc) rc = sb_launch(c, F_G2_LAYERNORM_ROWS, (unsigned)T, 1, 256, 0, s, l2, 0);
+            if (!rc) rc = sb_sgemm_nt_3xtf32(pa, (const float *)(uintptr_t)wfc, py, T, FC, C, s);
+            void *ga[] = {&e->pf_y, &bfc, &e->pf_a, &FC};
+            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_GELU, (unsigned)T, 1, 256, 0, s, ga, 0);
+            if (!rc) rc = sb_sgemm_nt_3xtf32(pa, (const float *)(uintptr_t)wp, py, T, C, FC, s);
+            void *pr[] = {&e->pf_y, &bp, &e->pf_x, &C};
+            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_RESID, (unsigned)T, 1, 256, 0, s, pr, 0);
+        }
+        if (rc) return rc;
+    }
+    SbStep st = e->st_begin;
+    st.pos = n;
+    return put_step(e, &st);
+}
+
 int sb_engine_prefill(sb_engine *e, int n) {
     if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);
-    SB_ARG(e->model == SB_MODEL_QWEN, "batched prefill is implemented for the Qwen engine");
     SB_ARG(n >= 0 && n < e->n_prompt, "prefill covers prompt tokens before the last one");
     if (n == 0) return 0;
+    if (e->model == SB_MODEL_GPT2) return prefill_gpt2(e, n);
     sb_ctx *c = e->c;
     if (!e->pf_x) {
         SB_CK(cuMemAlloc(&e->pf_x, (size_t)PF_T * QW_C * 4));
@@ -607,7 +664,7 @@ int sb_engine_prefill(sb_engine *e, int n) {
 int sb_engine_generate(sb_engine *e, const int *prompt, int n_prompt, int n_gen, int *out_ids, int *n_out,
                        unsigned gen_flags) {
     int rc = sb_engine_begin(e, prompt, n_prompt, n_gen, gen_flags);
-    if (!rc && e->model == SB_MODEL_QWEN && !(e->flags & SB_FLAG_NO_PREFILL) && n_prompt > 1) {
+    if (!rc && !(e->flags & SB_FLAG_NO_PREFILL) && n_prompt > 1) {
         rc = sb_engine_prefill(e, n_prompt - 1); /* prompt tokens batched on the tensor cores */
         if (!rc) rc = sb_engine_steps(e, n_gen + 1, 1); /* last prompt token + n_gen */
         if (!rc) rc = sb_engine_finish(e, out_ids, n_out);

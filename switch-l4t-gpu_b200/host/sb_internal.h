@@ -58,6 +58,11 @@ typedef enum {
     F_PF_ATTN,
     F_PF_RESID,
     F_PF_SWIGLU_SPLIT,
+    F_G2PF_EMBED,
+    F_G2PF_QKV,
+    F_G2PF_BIAS_RESID,
+    F_G2PF_BIAS_GELU,
+    F_G2_LAYERNORM_ROWS,
     F_COUNT
 } sb_fn_id;
 

@@ -245,6 +245,19 @@ static int encode_kmajor_f32(CUtensorMap *tm, const void *base, int K, int rows)
     return 0;
 }
 
+/* C = A . Bt^T with A [M][K] and Bt [N][K] both K-major (the kernel's operand form). */
+static int sgemm3x_launch(sb_ctx *c, const float *A, const float *Bt, float *C, int M, int N, int K, void *stream) {
+    CUtensorMap ta, tb;
+    int rc = encode_kmajor_f32(&ta, A, K, M);
+    if (!rc) rc = encode_kmajor_f32(&tb, Bt, K, N);
+    if (rc) return rc;
+    const long tiles = (long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128);
+    CUdeviceptr cc = DP(C);
+    void *args[] = {&ta, &tb, &cc, &M, &N, &K};
+    const unsigned smem = 1024 + 3 * 65536 + 256;
+    return sb_launch(c, F_SGEMM_3XTF32, (unsigned)tiles, 1, 192, smem, (CUstream)stream, args, 0);
+}
+
 int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream) {
     SB_ARG(A && B && C && M >= 0 && N >= 0 && K > 0, "bad sgemm_3xtf32 arguments");
     SB_ARG(K % 4 == 0 && N % 4 == 0 && ALIGNED16(A) && ALIGNED16(B) && ALIGNED16(C),
@@ -268,14 +281,18 @@ int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int 
     int rc = sb_launch(c, F_TRANSPOSE_F32, (unsigned)CEIL_DIV(N, 32), (unsigned)CEIL_DIV(K, 32), 32 * 8, 0,
                        (CUstream)stream, targs, 0);
     if (rc) return rc;
-    CUtensorMap ta, tb;
-    rc = encode_kmajor_f32(&ta, A, K, M);
-    if (!rc) rc = encode_kmajor_f32(&tb, (const void *)(uintptr_t)bt, K, N);
-    if (rc) return rc;
-    CUdeviceptr cc = DP(C);
-    void *args[] = {&ta, &tb, &cc, &M, &N, &K};
-    const unsigned smem = 1024 + 3 * 65536 + 256;
-    return sb_launch(c, F_SGEMM_3XTF32, (unsigned)tiles, 1, 192, smem, (CUstream)stream, args, 0);
+    return sgemm3x_launch(c, A, (const float *)(uintptr_t)bt, C, M, N, K, stream);
+}
+
+int sb_sgemm_nt_3xtf32(const float *A, const float *Bt, float *C, int M, int N, int K, void *stream) {
+    SB_ARG(A && Bt && C && M >= 0 && N >= 0 && K > 0, "bad sgemm_nt_3xtf32 arguments");
+    SB_ARG(K % 4 == 0 && N % 4 == 0 && ALIGNED16(A) && ALIGNED16(Bt) && ALIGNED16(C),
+           "sgemm_nt_3xtf32 needs K % 4 == 0, N % 4 == 0 and 16-byte aligned A, Bt, C");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (M == 0 || N == 0) return 0;
+    SB_ARG((long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128) < 0x7fffffffL, "sgemm_nt_3xtf32: too many tiles");
+    return sgemm3x_launch(c, A, Bt, C, M, N, K, stream);
 }
 
 int sb_tc_error(int *err) {

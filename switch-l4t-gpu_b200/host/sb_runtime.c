@@ -77,6 +77,11 @@ static const struct {
     [F_PF_ATTN] = {M_QWEN, "qwen_pf_attn"},
     [F_PF_RESID] = {M_QWEN, "qwen_pf_resid"},
     [F_PF_SWIGLU_SPLIT] = {M_QWEN, "qwen_pf_swiglu_split"},
+    [F_G2PF_EMBED] = {M_GPT2, "gpt2_pf_embed"},
+    [F_G2PF_QKV] = {M_GPT2, "gpt2_pf_qkv"},
+    [F_G2PF_BIAS_RESID] = {M_GPT2, "gpt2_pf_bias_resid"},
+    [F_G2PF_BIAS_GELU] = {M_GPT2, "gpt2_pf_bias_gelu"},
+    [F_G2_LAYERNORM_ROWS] = {M_GPT2, "layernorm"},
 };
 
 /* ---------------------------------------------------------------- errors */

@@ -151,3 +151,35 @@ def test_qwen_prefill_matches_stepwise_priming(cuda_dev, qwen_weights):
 def test_qwen_greedy_stepwise_priming(cuda_dev, qwen_weights):
     """The greedy check with the one-token-per-step prompt path."""
     _greedy(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 32, 63, 33, sb200.FLAG_NO_PREFILL)
+
+
+def test_gpt2_prefill_matches_stepwise_priming(cuda_dev, gpt2_weights):
+    """GPT-2 batched prefill (3xTF32 tensor-core products) vs one step per
+    prompt token and vs the oracle, at 16 and 140 prompt tokens."""
+    for n_prompt in (16, 140):
+        prompt = sb200.synth_ids(n_prompt, sb200.GPT2["V"], 60 + n_prompt)
+        eng = sb200.Engine(sb200.MODEL_GPT2, gpt2_weights, 256)
+        ref = orc.Model("gpt2", gpt2_weights, 256, sb200.GPT2["V"])
+        try:
+            outs = []
+            for mode in ("prefill", "steps"):
+                eng.begin(prompt, 4)
+                if mode == "prefill":
+                    eng.prefill(n_prompt - 1)
+                else:
+                    eng.steps(n_prompt - 1, False)
+                got = np.zeros(sb200.GPT2["V"], dtype=np.float32)
+                eng.forward(prompt[-1], n_prompt - 1, True, got)
+                outs.append(got)
+            for p, t in enumerate(prompt):
+                want = ref.forward(t, p, p == n_prompt - 1)
+            assert _rel(outs[0], outs[1]) <= LOGIT_TOL
+            assert _rel(outs[0], want) <= LOGIT_TOL, f"prefill vs oracle {_rel(outs[0], want):.2e}"
+            assert int(np.argmax(outs[0])) == int(np.argmax(want))
+        finally:
+            eng.close()
+            ref.close()
+
+
+def test_gpt2_greedy_stepwise_priming(cuda_dev, gpt2_weights):
+    _greedy(sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"], 16, 63, 17, sb200.FLAG_NO_PREFILL)
