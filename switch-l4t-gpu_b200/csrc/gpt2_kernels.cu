@@ -434,3 +434,6 @@ extern "C" __global__ void gpt2_pf_bias_gelu(const float *__restrict__ Y, const 
     for (int i = threadIdx.x; i < n; i += blockDim.x)
         A[(size_t)t * n + i] = gelu_ref(__fadd_rn(Y[(size_t)t * n + i], b[i]));
 }
+
+// The whole decode step as one persistent kernel.
+#include "gpt2_mk.cuh"

@@ -45,7 +45,7 @@ struct sb_engine {
     int V, NL, kvw;
     CUgraphExec gexec[2];
     int n_prompt, n_end;
-    /* persistent whole-step kernel (Qwen) */
+    /* persistent whole-step kernel (qwen_decode_mk / gpt2_decode_mk) */
     int mk;
     CUdeviceptr ll, sync, err; /* flagged exchange words; u32[2] seq / arrivals; error flag */
     int mk_splits, mk_score_cap;
@@ -59,11 +59,13 @@ struct sb_engine {
 
 #define MK_THREADS 512
 #define MK_WARPS 16
-static unsigned mk_smem_bytes(int score_cap) {
-    /* x planes (FC floats) | 16 warp regions of (6 rows + 1/2 row) of 896 fp16 | scores |
-     * red(32) opart(16x64) ksum(16) (m, l) of NH x SPLITS_MAX partials */
-    return (unsigned)(QW_FC * 4 + MK_WARPS * (6 * QW_C * 2 + QW_C) + score_cap * 4 +
-                      (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4);
+static unsigned mk_smem_bytes(int model, int score_cap) {
+    /* Qwen: x planes (FC floats) | 16 warp regions of (6 rows + 1/2 row) of 896 fp16
+     * GPT-2: x (FC floats) | 16 warp regions of (3 rows + 1/2 row) of 768 fp32
+     * both: | scores | red(32) opart(16x64) ksum(16) (m, l) of NH x SPLITS_MAX partials */
+    const unsigned head = model == SB_MODEL_QWEN ? QW_FC * 4 + MK_WARPS * (6 * QW_C * 2 + QW_C)
+                                                 : G2_FC * 4 + MK_WARPS * (3 * G2_C * 4 + G2_C * 2);
+    return head + (unsigned)score_cap * 4 + (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4;
 }
 
 /* ------------------------------------------------------------------ upload */
@@ -222,6 +224,8 @@ static int launch_kernel(sb_engine *e, int l, int which, int with_logits, int pd
                                      : launch_gpt2(e, l, which, with_logits, pdl);
 }
 
+static int mk_fn(int model) { return model == SB_MODEL_QWEN ? F_QWEN_MK : F_GPT2_MK; }
+
 static int record_mk(sb_engine *e, int with_logits) {
     SbMkParams prm;
     memset(&prm, 0, sizeof prm);
@@ -239,7 +243,7 @@ static int record_mk(sb_engine *e, int with_logits) {
     prm.splits = e->mk_splits;
     prm.score_cap = e->mk_score_cap;
     void *args[] = {&prm};
-    return sb_launch_coop(e->c, F_QWEN_MK, (unsigned)e->c->sms, MK_THREADS, e->mk_smem, e->stream, args);
+    return sb_launch_coop(e->c, mk_fn(e->model), (unsigned)e->c->sms, MK_THREADS, e->mk_smem, e->stream, args);
 }
 
 static int record_model(sb_engine *e, int with_logits) {
@@ -308,14 +312,14 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     e->max_splits = CEIL_DIV(max_ctx, 16);
     /* the persistent kernel needs >= 128 co-resident CTAs (its per-CTA row
      * shares are sized for that) and cooperative launch */
-    if (model == SB_MODEL_QWEN && !(flags & SB_FLAG_MULTI_KERNEL) && c->sms >= 128) {
-        e->mk_splits = c->sms / QW_NH;
+    if (!(flags & SB_FLAG_MULTI_KERNEL) && c->sms >= 128) {
+        e->mk_splits = c->sms / (model == SB_MODEL_QWEN ? QW_NH : G2_NH);
         if (e->mk_splits > SB_MK_SPLITS_MAX) e->mk_splits = SB_MK_SPLITS_MAX;
         e->mk_score_cap = (CEIL_DIV(max_ctx, e->mk_splits) + 8 + 3) & ~3; /* multiple of 4 floats */
-        e->mk_smem = mk_smem_bytes(e->mk_score_cap);
+        e->mk_smem = mk_smem_bytes(model, e->mk_score_cap);
         int coop = 0;
         cuDeviceGetAttribute(&coop, CU_DEVICE_ATTRIBUTE_COOPERATIVE_LAUNCH, c->dev);
-        e->mk = coop && sb_occupancy(c, F_QWEN_MK, MK_THREADS, e->mk_smem) >= 1;
+        e->mk = coop && sb_occupancy(c, mk_fn(model), MK_THREADS, e->mk_smem) >= 1;
     }
     const int groups = qw ? QW_NKV : G2_NH, G = qw ? QW_NH / QW_NKV : 1;
     const int C = qw ? QW_C : G2_C, FC = qw ? QW_FC : G2_FC, NQ = qw ? QW_C : G2_C;

@@ -63,6 +63,7 @@ typedef enum {
     F_G2PF_BIAS_RESID,
     F_G2PF_BIAS_GELU,
     F_G2_LAYERNORM_ROWS,
+    F_GPT2_MK,
     F_COUNT
 } sb_fn_id;
 

@@ -82,6 +82,7 @@ static const struct {
     [F_G2PF_BIAS_RESID] = {M_GPT2, "gpt2_pf_bias_resid"},
     [F_G2PF_BIAS_GELU] = {M_GPT2, "gpt2_pf_bias_gelu"},
     [F_G2_LAYERNORM_ROWS] = {M_GPT2, "layernorm"},
+    [F_GPT2_MK] = {M_GPT2, "gpt2_decode_mk"},
 };
 
 /* ---------------------------------------------------------------- errors */

@@ -51,9 +51,38 @@ def test_qwen_default_is_persistent(cuda_dev, qwen_weights):
         eng.close()
 
 
-def test_gpt2_teacher_forced(cuda_dev, gpt2_weights):
+@pytest.mark.parametrize("flags", [0, sb200.FLAG_MULTI_KERNEL])
+def test_gpt2_teacher_forced(cuda_dev, gpt2_weights, flags):
+    """flags 0: the persistent whole-step kernel; MULTI_KERNEL: one kernel per stage."""
     ids = sb200.synth_ids(12, sb200.GPT2["V"], 8)
-    _teacher_forced(sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"], 64, ids)
+    _teacher_forced(sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"], 64, ids, flags)
+
+
+def test_gpt2_default_is_persistent(cuda_dev, gpt2_weights):
+    eng = sb200.Engine(sb200.MODEL_GPT2, gpt2_weights, 64)
+    try:
+        assert eng.persistent == (sb200.sm_count() >= 128)
+        assert eng.launches_per_step() == (1 if eng.persistent else 63)
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("model", ["qwen", "gpt2"])
+def test_persistent_graph_matches_direct(cuda_dev, qwen_weights, gpt2_weights, model):
+    """The persistent kernel replayed from a graph and launched directly give
+    bit-identical logits."""
+    mid, w, V = ((sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"]) if model == "qwen"
+                 else (sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"]))
+    ids = sb200.synth_ids(5, V, 19)
+    outs = []
+    for f in (0, sb200.FLAG_NO_GRAPH):
+        eng = sb200.Engine(mid, w, 32, f)
+        got = np.zeros(V, dtype=np.float32)
+        for p, t in enumerate(ids):
+            eng.forward(t, p, p == len(ids) - 1, got if p == len(ids) - 1 else None)
+        outs.append(got)
+        eng.close()
+    assert np.array_equal(outs[0], outs[1])
 
 
 @pytest.mark.parametrize("base,flags", [(0, sb200.FLAG_NO_GRAPH),
@@ -97,9 +126,44 @@ def test_qwen_greedy_64(cuda_dev, qwen_weights, flags):
     _greedy(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 32, 63, 32, flags)
 
 
-def test_gpt2_greedy_64(cuda_dev, gpt2_weights):
+@pytest.mark.parametrize("flags", [0, sb200.FLAG_MULTI_KERNEL])
+def test_gpt2_greedy_64(cuda_dev, gpt2_weights, flags):
     """configs[1] shape: 16 seeded prompt tokens, greedy, 64 steps identical."""
-    _greedy(sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"], 16, 63, 16)
+    _greedy(sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"], 16, 63, 16, flags)
+
+
+@pytest.mark.parametrize("model", ["qwen", "gpt2"])
+def test_long_context_decode(cuda_dev, qwen_weights, gpt2_weights, model):
+    """A 600-token prompt (batched prefill), then 4 teacher-forced decode
+    steps against the oracle, for the persistent kernel and the per-stage
+    kernels: 8 attention T-splits of 75 positions each, so the persistent
+    kernel's shared-memory score path (positions past 64 per split) runs."""
+    mid, w, V = ((sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"]) if model == "qwen"
+                 else (sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"]))
+    n_prompt, ctx, n_dec = 600, 640, 4
+    prompt = sb200.synth_ids(n_prompt, V, 600)
+    ref = orc.Model(model, w, ctx, V)
+    try:
+        for p, t in enumerate(prompt[:-1]):
+            ref.forward(t, p, False)
+        toks, wants = [prompt[-1]], []
+        for k in range(n_dec):
+            wants.append(ref.forward(toks[-1], n_prompt - 1 + k, True))
+            toks.append(int(np.argmax(wants[-1])))
+    finally:
+        ref.close()
+    for flags in (0, sb200.FLAG_MULTI_KERNEL):
+        eng = sb200.Engine(mid, w, ctx, flags)
+        try:
+            eng.begin(prompt, n_dec)
+            eng.prefill(n_prompt - 1)
+            for k in range(n_dec):
+                got = np.zeros(V, dtype=np.float32)
+                eng.forward(toks[k], n_prompt - 1 + k, True, got)
+                assert _rel(got, wants[k]) <= LOGIT_TOL, f"flags {flags} step {k}: {_rel(got, wants[k]):.2e}"
+                assert int(np.argmax(got)) == toks[k + 1]
+        finally:
+            eng.close()
 
 
 def test_engine_rejects_bad_input(cuda_dev, gpt2_weights, tmp_path):
