@@ -23,8 +23,11 @@ needed between timed steps.
 Secondary keys of the same line: "sgemm" -- 16384^3 FP32 SGEMM sharded by
 row panels over all ranks (strong scaling) with the NCCL all-gather of C,
 compute-only and with the gather, per-GPU fraction of the live FP32 FMA
-peak; "sgemm_3xtf32" -- the same on the opt-in 3xTF32 tensor-core kernel; "gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4
-and 16 on the tcgen05 tensor cores) in GB/s against the HBM peak.
+peak; "sgemm_3xtf32" -- the same on the opt-in 3xTF32 tensor-core kernel;
+"gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4 and 16
+on the tcgen05 tensor cores) in GB/s against the HBM peak; "gpt2_decode" --
+configs[1], GPT-2-124M-shape FP32 decode (16 prompt tokens, 128 new), with
+its own e2e, roofline and reference CPU baseline.
 
 `--impl reference` times the reference's own CPU decode (cpu_forward of
 gpu-llm/engine/qwen_engine.c compiled unmodified into oracle/_ref) on the
@@ -317,6 +320,116 @@ def sgemm_section(torch, dev, dist_on, steps, warmup, kernel="fp32"):
     return res
 
 
+GPT2_SEED, GPT2_PROMPT, GPT2_GEN, GPT2_CTX = 20261202, 16, 128, 1024
+GPT2_CPU_TOKENS = 48  # per host core: about 10 s of reference CPU decode
+
+
+def gpt2_section(torch, dev, dist, steps, warmup, with_cpu):
+    """GPT-2-124M-shape FP32 greedy decode, 16 seeded
+    prompt tokens, 128 new tokens, batch 1 -- the same measurements as the
+    headline (resident decode, e2e through sb_engine_generate, roofline of
+    the step kernel, reference CPU decode on the host cores)."""
+    import ctypes
+    import sb200
+
+    def barrier():
+        if dist:
+            import torch.distributed as tdist
+            tdist.barrier()
+
+    d = os.path.dirname(weights_path())
+    path = os.path.join(d, f"gpt2_{GPT2_SEED}.bin")
+    if LOCAL_RANK == 0 and not (os.path.exists(path) and os.path.getsize(path) == sb200.GPT2["TOTAL_FLOATS"] * 4):
+        tmp = path + f".tmp{os.getpid()}"
+        sb200.synth_weights(sb200.MODEL_GPT2, tmp, GPT2_SEED)
+        os.replace(tmp, path)
+    barrier()
+    V = sb200.GPT2["V"]
+    eng = sb200.Engine(sb200.MODEL_GPT2, path, GPT2_CTX)
+    ext = torch.cuda.ExternalStream(eng.stream, device=dev)
+    prompt = sb200.synth_ids(GPT2_PROMPT, V, 2000 + RANK)
+
+    def decode_step():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        eng.begin(prompt, GPT2_GEN)
+        eng.steps(GPT2_PROMPT - 1, False)
+        eng.steps(1, True)
+        e0.record(ext)
+        eng.steps(GPT2_GEN, True)
+        e1.record(ext)
+        ids = eng.finish(GPT2_PROMPT + GPT2_GEN + 1)
+        assert len(ids) == GPT2_PROMPT + GPT2_GEN + 1
+        return e0.elapsed_time(e1)
+
+    pin_in = torch.tensor(prompt, dtype=torch.int32).pin_memory()
+    pin_out = torch.zeros(GPT2_PROMPT + GPT2_GEN + 1, dtype=torch.int32).pin_memory()
+    L = sb200.lib()
+    nout = ctypes.c_int()
+
+    def e2e_step():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ext)
+        sb200.check(L.sb_engine_generate(eng.h, ctypes.c_void_p(pin_in.data_ptr()), GPT2_PROMPT, GPT2_GEN,
+                                         ctypes.c_void_p(pin_out.data_ptr()), ctypes.byref(nout), 0))
+        e1.record(ext)
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    for _ in range(warmup):
+        decode_step()
+    torch.cuda.synchronize()
+    barrier()
+    ms = [decode_step() for _ in range(steps)]
+    for _ in range(max(1, warmup // 2)):
+        e2e_step()
+    barrier()
+    e2e_ms = [e2e_step() for _ in range(steps)]
+    tot = torch.tensor([sum(ms), sum(e2e_ms)], dtype=torch.float64, device=dev)
+    if dist:
+        import torch.distributed as tdist
+        tdist.all_reduce(tot, op=tdist.ReduceOp.MAX)
+    total_ms, e2e_total = float(tot[0].item()), float(tot[1].item())
+    value = WORLD * steps * GPT2_GEN / (total_ms / 1e3)
+    peaks = measured_peaks()
+    peak = float(peaks["hbm_gbs"]) if peaks and peaks.get("hbm_gbs") else FALLBACK_HBM_GBS
+    tok_ms = total_ms / (steps * GPT2_GEN)
+    step_bytes = eng.step_bytes()
+    achieved = step_bytes / (tok_ms * 1e-3) / 1e9
+    dom = "gpt2_decode_mk" if eng.persistent else "gpt2 per-stage kernels"
+    out = {
+        "metric": "GPT-2-124M-shape FP32 decode tok/s", "value": round(value, 2), "unit": UNIT,
+        "ms_per_step": round(total_ms / steps, 3), "steps": steps, "dtype": "f32",
+        "config": {"workload": "gpt2-124m-fp32-decode (configs[1])", "n_prompt": GPT2_PROMPT, "n_gen": GPT2_GEN,
+                   "batch": 1, "max_ctx": GPT2_CTX,
+                   "weights": "random-init N(0,0.02) fp32 in the reference file layout (497,759,232 B)"},
+        "e2e": {"value": round(WORLD * steps * GPT2_GEN / (e2e_total / 1e3), 2), "unit": UNIT,
+                "h2d_bytes_per_step": GPT2_PROMPT * 4 + 48, "d2h_bytes_per_step": (GPT2_PROMPT + GPT2_GEN + 1) * 4 + 48,
+                "note": "sb_engine_generate: prompt from pinned host memory, batched 3xTF32 prefill of the first "
+                        "15 prompt tokens, 129 decode steps, ids back"},
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic().get("gpt2_decode_mk") if eng.persistent
+                     else None, "bytes_per_launch": step_bytes, "launch_us": round(tok_ms * 1e3, 2)},
+        "gpu_launches": steps * GPT2_GEN * eng.launches_per_step(True),
+        "step_kernel": "persistent whole-step kernel (1 cooperative launch per token)" if eng.persistent
+        else "one kernel per stage (63 launches per token)",
+    }
+    eng.close()
+    exe = os.path.join(REPO, "oracle", "_ref", "ref_gpt2_bench")
+    if with_cpu and RANK == 0 and WORLD == 1 and os.access(exe, os.X_OK):
+        try:
+            cores = host_cores()
+            r = subprocess.run([exe, path, str(cores), "0", "1", str(GPT2_CPU_TOKENS), "42"],
+                               capture_output=True, text=True, timeout=900)
+            j = json.loads(r.stdout.strip().splitlines()[-1])
+            out["cpu_baseline"] = {"value": round(j["tok_s"], 4), "unit": UNIT, "cores": cores, "kind": "reference",
+                                   "sample": f"{cores} forked replicas of the reference cpu_forward "
+                                             f"(gpt2_engine.c:363-421) + argmax, {GPT2_CPU_TOKENS} greedy decode "
+                                             f"tokens each; {j['timed_s']:.1f} s wall"}
+        except Exception as ex:  # reported, not fatal
+            out["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+    return out
+
+
 def gemv_section(torch, dev):
     """Standalone FP16 GEMV sweep y = W.x (fp16 W and x, fp32 y) at batch 1
     (CUDA cores), 4 and 16 (tcgen05 tensor cores); W copies rotated through
@@ -499,6 +612,7 @@ def run_b200(args):
         line["sgemm"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3)
         line["sgemm_3xtf32"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3, kernel="3xtf32")
         line["gemv"] = gemv_section(torch, dev)
+        line["gpt2_decode"] = gpt2_section(torch, dev, dist, max(3, args.steps // 2), 3, not args.no_cpu_baseline)
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_baseline(path)

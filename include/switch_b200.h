@@ -150,8 +150,8 @@ typedef struct sb_engine sb_engine;
 #define SB_MODEL_GPT2 2
 #define SB_FLAG_NO_GRAPH 1u  /* launch kernels directly instead of graph replay */
 #define SB_FLAG_NO_PDL 2u    /* no programmatic dependent launch            */
-#define SB_FLAG_MULTI_KERNEL 4u /* Qwen: one kernel per stage instead of the
-                                 * persistent whole-step kernel              */
+#define SB_FLAG_MULTI_KERNEL 4u /* one kernel per stage instead of the
+                                 * persistent whole-step kernel (both models) */
 #define SB_FLAG_NO_PREFILL 8u /* sb_engine_generate primes the prompt one token
                                * per step instead of sb_engine_prefill        */
 #define SB_GEN_STOP_EOS 1u   /* stop at the model's end tokens (reference behaviour) */

@@ -52,6 +52,8 @@ constexpr int LL_X = 0, LL_QKV = LL_X + C, LL_HID = LL_QKV + QKV, LL_PART = LL_H
 static_assert(LL_PART + NH * SPLITS_MAX * PW <= SB_MK_LL_WORDS, "flagged-word area");
 static_assert(LL_QKV % 2 == 0 && LL_HID % 2 == 0 && LL_PART % 2 == 0, "pairs stay 16-byte aligned");
 constexpr int HID_PAIRS = (FC / 2 + THREADS - 1) / THREADS;  // 3
+static_assert(C >= THREADS && NH * SPLITS_MAX <= THREADS,
+              "the combine polls each (m, l) pair with the o words of dim tid");
 
 // R fp32 rows at base + r*stride (float4 units) against x (float4 chunks),
 // chunk range [c0, c1), row data starting at chunk row_c0; per-lane partials.
@@ -310,15 +312,27 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
             }
             float2 *qkv_s = reinterpret_cast<float2 *>(opart);
             bool ok = true;
-            if (warp == 0) {
-                float2 v;
-                ok = ll_wait2(llqkv + h * HD + 2 * lane, e_qkv, v.x, v.y, p.err);
-                qkv_s[lane] = v;
-                if (t1 == T) {
-                    ok = ok && ll_wait2(kcur, e_qkv, v.x, v.y, p.err);
-                    qkv_s[32 + lane] = v;
-                    ok = ok && ll_wait2(vcur, e_qkv, v.x, v.y, p.err);
-                    qkv_s[64 + lane] = v;
+            if (warp == 0) {  // q (and the current k, v) requested together: one round trip
+                const bool cur = t1 == T;
+                const u64 *qw = llqkv + h * HD + 2 * lane;
+                for (long spin = 0;; spin++) {
+                    u64 w[6];
+                    ll_get2(qw, w[0], w[1]);
+                    if (cur) {
+                        ll_get2(kcur, w[2], w[3]);
+                        ll_get2(vcur, w[4], w[5]);
+                    }
+                    bool all = ll_is(w[0], e_qkv) && ll_is(w[1], e_qkv);
+                    if (cur) all = all && ll_is(w[2], e_qkv) && ll_is(w[3], e_qkv) && ll_is(w[4], e_qkv) && ll_is(w[5], e_qkv);
+                    if (all) {
+                        qkv_s[lane] = make_float2(ll_val(w[0]), ll_val(w[1]));
+                        if (cur) {
+                            qkv_s[32 + lane] = make_float2(ll_val(w[2]), ll_val(w[3]));
+                            qkv_s[64 + lane] = make_float2(ll_val(w[4]), ll_val(w[5]));
+                        }
+                        break;
+                    }
+                    if (!ll_keep_polling(spin, p.err)) { ok = false; break; }
                 }
             }
             if (__syncthreads_or(!ok)) { aborted = true; break; }
@@ -406,13 +420,10 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
         {
             const unsigned e = epoch(l, 1);
             bool ok = true;
-            for (int it = tid; it < NH * nsplit; it += THREADS) {
-                const int h = it / nsplit, s = it % nsplit;
-                float mv, lv;
-                ok = ok && ll_wait2(llpart + (long)(h * SPLITS_MAX + s) * PW + HD, e, mv, lv, p.err);
-                mlv[2 * it] = mv;
-                mlv[2 * it + 1] = lv;
-            }
+            // this thread's (m, l) pair (item tid < NH*nsplit <= THREADS) is
+            // polled together with its o words below
+            const u64 *mlw = llpart + (long)((tid / nsplit) * SPLITS_MAX + tid % nsplit) * PW + HD;
+            bool ml_done = tid >= NH * nsplit;
             float ov[2][SPLITS_MAX];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
@@ -421,6 +432,8 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
                 const u64 *base = llpart + (long)((d / HD) * SPLITS_MAX) * PW + (d % HD);
                 for (long spin = 0; ok; spin++) {
                     bool all = true;
+                    u64 m0 = 0ull, m1 = 0ull;
+                    if (!ml_done) ll_get2(mlw, m0, m1);
 #pragma unroll
                     for (int s = 0; s < SPLITS_MAX; s++) {
                         ov[u][s] = 0.f;
@@ -428,6 +441,15 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
                             const u64 wv = ll_get(base + (long)s * PW);
                             all = all && ll_is(wv, e);
                             ov[u][s] = ll_val(wv);
+                        }
+                    }
+                    if (!ml_done) {
+                        if (ll_is(m0, e) && ll_is(m1, e)) {
+                            mlv[2 * tid] = ll_val(m0);
+                            mlv[2 * tid + 1] = ll_val(m1);
+                            ml_done = true;
+                        } else {
+                            all = false;
                         }
                     }
                     if (all) break;

@@ -72,6 +72,8 @@ constexpr int LL_WORDS = LL_PART + NH * SPLITS_MAX * PW;
 static_assert(LL_WORDS == SB_MK_LL_WORDS, "flagged-word layout");
 static_assert(LL_QKV % 2 == 0 && LL_HID % 2 == 0 && LL_PART % 2 == 0 && PW % 2 == 0, "pairs stay 16-byte aligned");
 constexpr int HID_PAIRS = (FC / 2 + THREADS - 1) / THREADS;  // hid word pairs per thread (5)
+static_assert(C >= THREADS && NH * SPLITS_MAX <= THREADS,
+              "the combine polls each (m, l) pair with the o words of dim tid");
 
 using namespace mkc;
 
@@ -488,14 +490,10 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         {
             const unsigned e = epoch(l, 1);
             bool ok = true;
-            // (m, l) of every partial into shared memory
-            for (int it = tid; it < NH * nsplit; it += THREADS) {
-                const int h = it / nsplit, s = it % nsplit;
-                float mv, lv;
-                ok = ok && ll_wait2(llpart + (long)(h * SPLITS_MAX + s) * PW + HD, e, mv, lv, p.err);
-                mlv[2 * it] = mv;
-                mlv[2 * it + 1] = lv;
-            }
+            // this thread's (m, l) pair (item tid < NH*nsplit <= THREADS) is
+            // polled together with its o words below
+            const u64 *mlw = llpart + (long)((tid / nsplit) * SPLITS_MAX + tid % nsplit) * PW + HD;
+            bool ml_done = tid >= NH * nsplit;
             // the o words of this thread's dims d = tid and tid + THREADS,
             // all splits requested before any is checked
             float ov[2][SPLITS_MAX];
@@ -506,6 +504,8 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                 const u64 *base = llpart + (long)((d / HD) * SPLITS_MAX) * PW + (d % HD);
                 for (long spin = 0; ok; spin++) {
                     bool all = true;
+                    u64 m0 = 0ull, m1 = 0ull;
+                    if (!ml_done) ll_get2(mlw, m0, m1);
 #pragma unroll
                     for (int s = 0; s < SPLITS_MAX; s++) {
                         ov[u][s] = 0.f;
@@ -513,6 +513,15 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                             const u64 wv = ll_get(base + (long)s * PW);
                             all = all && ll_is(wv, e);
                             ov[u][s] = ll_val(wv);
+                        }
+                    }
+                    if (!ml_done) {
+                        if (ll_is(m0, e) && ll_is(m1, e)) {
+                            mlv[2 * tid] = ll_val(m0);
+                            mlv[2 * tid + 1] = ll_val(m1);
+                            ml_done = true;
+                        } else {
+                            all = false;
                         }
                     }
                     if (all) break;
