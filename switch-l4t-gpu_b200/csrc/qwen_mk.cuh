@@ -63,7 +63,8 @@ constexpr int CPR = C / 8;            // 16-byte chunks per K=896 row (112)
 constexpr int CPR_D = FC / 8;         // chunks per K=4864 row (608)
 constexpr int WHEAD = 6 * C * 2;      // per-warp head slot: 6 rows of 896 fp16 (S1, S4, S5, LM head)
 constexpr int WREG = WHEAD + C;       // + tail slot for the O half-row (896 B): 11648 B per warp
-constexpr int LM_NB = 3;              // LM-head rows in flight per warp
+constexpr int LM_G = 3;               // LM-head rows a warp reduces together (one group)
+constexpr int LM_NB = 2;              // LM-head groups in flight per warp (2 x 3 rows = the head slot)
 constexpr int SPLITS_MAX = SB_MK_SPLITS_MAX;
 constexpr int PW = HD + 2;            // words per attention partial: o[64], m, l
 // flagged-word layout (u64 words)
@@ -642,6 +643,25 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     }
     // ================= LM head + argmax
     if (p.with_logits) {
+        int v0, v1;
+        share(V, b, G, v0, v1);
+        // per warp: rows v0 + warp + 16j, LM_G at a time (one group: one
+        // dot pass over x and LM_G independent reductions), through LM_NB
+        // groups of row buffers in the head slot, each group filled by bulk
+        // copies completing on its own mbarrier.  The first groups are
+        // requested before the final norm's input arrives.
+        const int nrow = max(0, (v1 - v0 - warp + WARPS - 1) / WARPS);
+        const int ngrp = (nrow + LM_G - 1) / LM_G;
+        auto issue_grp = [&](int k) {  // lane 0
+            const int slot = k % LM_NB, j0 = k * LM_G, nj = min(LM_G, nrow - j0);
+            issue_begin(2 + slot, (unsigned)nj * C * 2);
+            for (int j = 0; j < nj; j++)
+                bulk_g2s(wreg + (slot * LM_G + j) * C * 2, emb + (long)(v0 + warp + WARPS * (j0 + j)) * C, C * 2,
+                         &mb[2 + slot]);
+        };
+        fence_async();
+        if (lane == 0)
+            for (int k = 0; k < min(LM_NB, ngrp); k++) issue_grp(k);
         const unsigned gwf = xact ? *reinterpret_cast<const unsigned *>(p.w + OFF_LNF / 2 + 2 * tid) : 0u;
         if (tid == 0) best_s = 0ull;
         if (!wait_x(epoch(NL - 1, 4))) {
@@ -652,37 +672,27 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         }
         rms_regs(xv, gwf, xlo, xhi, red, eps);
         __syncthreads();
-        int v0, v1;
-        share(V, b, G, v0, v1);
-        // per warp: rows v0 + warp + 16k through a ring of LM_NB row buffers,
-        // each filled by a bulk copy completing on its own mbarrier
         unsigned long long best = 0ull;
-        fence_async();
-        for (int k = 0; k < LM_NB; k++) {
-            const int r = v0 + warp + WARPS * k;
-            if (r < v1 && lane == 0) {
-                issue_begin(2 + k, C * 2);
-                bulk_g2s(wreg + k * C * 2, emb + (long)r * C, C * 2, &mb[2 + k]);
-            }
-        }
-        for (int k = 0;; k++) {
-            const int r = v0 + warp + WARPS * k;
-            if (r >= v1) break;
-            const int slot = k % LM_NB;
+        for (int k = 0; k < ngrp; k++) {
+            const int slot = k % LM_NB, j0 = k * LM_G, nj = min(LM_G, nrow - j0);
             wait_slot(2 + slot);
             __syncwarp();
-            float a[1];
-            smem_rows_dot<1>(wreg4 + slot * CPR, 0, 1, xlo, xhi, 0, CPR, 0, a);
-            const float dotv = warp_sum(a[0]);
-            if (lane == 0) p.logits[r] = dotv;
-            const unsigned long long key = argmax_key(dotv, r);
-            best = key > best ? key : best;
+            float a[LM_G];
+            smem_rows_dot<LM_G>(wreg4 + slot * LM_G * CPR, CPR, nj, xlo, xhi, 0, CPR, 0, a);
+#pragma unroll
+            for (int j = 0; j < LM_G; j++) {
+                const float dotv = warp_sum(a[j]);
+                if (j < nj) {
+                    const int r = v0 + warp + WARPS * (j0 + j);
+                    if (lane == 0) p.logits[r] = dotv;
+                    const unsigned long long key = argmax_key(dotv, r);
+                    best = key > best ? key : best;
+                }
+            }
             __syncwarp();
-            const int rn = v0 + warp + WARPS * (k + LM_NB);
-            if (rn < v1 && lane == 0) {
+            if (k + LM_NB < ngrp && lane == 0) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue_begin(2 + slot, C * 2);
-                bulk_g2s(wreg + slot * C * 2, emb + (long)rn * C, C * 2, &mb[2 + slot]);
+                issue_grp(k + LM_NB);
             }
         }
         if (lane == 0 && best) atomicMax(&best_s, best);
