@@ -42,10 +42,6 @@ constexpr int ROWB = C * 4;           // bytes of one K=768 row (3072)
 constexpr int WHEAD = 3 * ROWB;       // per-warp slot: 3 rows (QKV, fc, proj half, LM ring)
 constexpr int WREG = WHEAD + ROWB / 2;// + the O half-row: 10752 B per warp
 constexpr int LM_NB = 3;
-// The first LM_PF_LAYERS * LM_PF_ROWS LM-head rows of each CTA are
-// prefetched into L2 during the last layers (87 MB over 148 CTAs: the tied
-// FP32 table is 154 MB, larger than L2, so only its head is warmed).
-constexpr int LM_PF_LAYERS = 3, LM_PF_ROWS = 64;
 constexpr int SPLITS_MAX = SB_MK_SPLITS_MAX;
 constexpr int PW = HD + 2;
 constexpr int LL_X = 0, LL_QKV = LL_X + C, LL_HID = LL_QKV + QKV, LL_PART = LL_HID + FC;
@@ -258,15 +254,9 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
         stamp(l, 0, 0);
         ln_regs(xv, L + L_LN1W, L + L_LN1B, xs, red, eps);
         __syncthreads();
-        if (prefetcher) {
-            prefetch_piece(l + 1, 0);
-            if (p.with_logits && l >= NL - LM_PF_LAYERS) {
-                int v0, v1;
-                share(V, b, G, v0, v1);
-                const long r0 = v0 + (long)(l - (NL - LM_PF_LAYERS)) * LM_PF_ROWS, r1 = min((long)v1, r0 + LM_PF_ROWS);
-                prefetch_rows(wte, ROWB, r0, r1, 1L << 20);
-            }
-        }
+        // (An L2 prefetch of the LM-head rows during the last layers measured
+        // 5 us per token slower: it competes with those layers' weights.)
+        if (prefetcher) prefetch_piece(l + 1, 0);
         wait_slot(0);
         __syncwarp();
         {

@@ -323,15 +323,9 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         stamp(l, 0, 0);
         rms_regs(xv, gw1, xlo, xhi, red, eps);
         __syncthreads();
-        if (prefetcher) {
-            prefetch_piece(l + 1, 0);
-            if (p.with_logits && l >= NL - 4) {  // first ~512 KB of this CTA's LM-head rows
-                int v0, v1;
-                share(V, b, G, v0, v1);
-                const long r0 = v0 + (long)(l - (NL - 4)) * 73, r1 = min((long)v1, r0 + 73);
-                prefetch_rows(emb, C * 2, r0, r1, 1L << 20);
-            }
-        }
+        // (An L2 prefetch of the LM-head rows during the last layers measured
+        // 10 us per token slower: it competes with those layers' weights.)
+        if (prefetcher) prefetch_piece(l + 1, 0);
         wait_slot(0);
         __syncwarp();
         if (pp1 < qp1) {
