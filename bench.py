@@ -27,7 +27,9 @@ peak; "sgemm_3xtf32" -- the same on the opt-in 3xTF32 tensor-core kernel;
 "gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4 and 16
 on the tcgen05 tensor cores) in GB/s against the HBM peak; "gpt2_decode" --
 configs[1], GPT-2-124M-shape FP32 decode (16 prompt tokens, 128 new), with
-its own e2e, roofline and reference CPU baseline.
+its own e2e, roofline and reference CPU baseline; "sgemm_1024" -- configs[0]
+(1024^3) beside the harness's CPU triple loop, and the CPU cpu_gemv_h per
+GEMV shape under "gemv" (rank 0, N = 1).
 
 `--impl reference` times the reference's own CPU decode (cpu_forward of
 gpu-llm/engine/qwen_engine.c compiled unmodified into oracle/_ref) on the
@@ -467,6 +469,68 @@ def gemv_section(torch, dev):
             "peak": peak, "unit": "GB/s", "shapes": out}
 
 
+def cpu_paths_baseline(torch, dev):
+    """configs[0] and configs[3] beside their reference CPU paths, timed on
+    the host cores (rank 0, N = 1): the harness's SGEMM triple loop
+    (gpu_workload.c:97-98) at 1024^3 and cpu_gemv_h (qwen_engine.c:276-284)
+    per GEMV shape, each as the oracle's C restatement, on one thread and
+    row-parallel over all cores (arithmetic unchanged)."""
+    import ctypes
+    import numpy as np
+    import sb200
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    import orc
+    cores = host_cores()
+    rng = np.random.default_rng(0)
+    n = 1024
+    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    B = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    rows1 = 64  # single-thread sample: 1/16 of the rows
+    t0 = time.perf_counter()
+    orc.sgemm(A, B, 0, rows1, nthreads=1)
+    g1 = 2.0 * rows1 * n * n / (time.perf_counter() - t0) / 1e9
+    t0 = time.perf_counter()
+    orc.sgemm(A, B, 0, n, nthreads=cores)
+    gall = 2.0 * n ** 3 / (time.perf_counter() - t0) / 1e9
+    dA, dB = torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev)
+    dC = torch.empty(n, n, device=dev)
+    for _ in range(5):
+        sb200.sgemm(dA, dB, dC, n, n, n)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 100
+    e0.record()
+    for _ in range(reps):
+        sb200.sgemm(dA, dB, dC, n, n, n)
+    e1.record()
+    e1.synchronize()
+    gpu_tf = 2.0 * n ** 3 / (e0.elapsed_time(e1) / reps * 1e-3) / 1e12
+    out = {"sgemm_1024": {
+        "metric": "SGEMM TFLOPS", "n": n, "value": round(gpu_tf, 2), "unit": "TFLOP/s",
+        "config": "configs[0]: 1024^3 FP32, A and B U[-1,1] from seed 0 (inputs L2-resident: 12 MB)",
+        "cpu_baseline": {"value": round(gall / 1e3, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "gflops_1_thread": round(g1, 3), "gflops_all_cores": round(gall, 2),
+                         "sample": f"oracle restatement of the harness triple loop: {rows1} rows on 1 thread, "
+                                   f"all 1024 rows row-parallel on {cores} threads"}}}
+    gem = {}
+    L = orc.oracle()
+    for (N, K) in GEMV_SHAPES:
+        W = rng.normal(0, 0.02, (N, K)).astype(np.float16).view(np.uint16)
+        x = rng.normal(0, 1, K).astype(np.float32)
+        y = np.zeros(N, dtype=np.float32)
+        res = {}
+        for label, th in (("1_thread", 1), ("all_cores", cores)):
+            t0 = time.perf_counter()
+            L.orc_gemv_h(W.ctypes.data_as(ctypes.c_void_p), x.ctypes.data_as(ctypes.c_void_p), None,
+                         y.ctypes.data_as(ctypes.c_void_p), K, N, th)
+            dt = time.perf_counter() - t0
+            res[f"GB/s_{label}"] = round((N * K * 2 + K * 4 + N * 4) / dt / 1e9, 2)
+        gem[f"{N}x{K}_b1"] = res
+    out["gemv_cpu"] = {"kind": "port", "cores": cores,
+                       "sample": "oracle restatement of cpu_gemv_h (fp16 W, fp32 x), whole matrix per shape",
+                       "shapes": gem}
+    return out
+
+
 # ------------------------------------------------------------------ GPU arm
 def run_b200(args):
     import torch
@@ -618,6 +682,13 @@ def run_b200(args):
             line["cpu_baseline"] = cpu_baseline(path)
         except Exception as ex:  # reported, not fatal
             line["cpu_baseline"] = {"value": None, "error": str(ex)[:200]}
+        if not args.no_secondary:
+            try:
+                extra = cpu_paths_baseline(torch, dev)
+                line["sgemm_1024"] = extra["sgemm_1024"]
+                line["gemv"]["cpu_baseline"] = extra["gemv_cpu"]
+            except Exception as ex:  # reported, not fatal
+                line["sgemm_1024"] = {"error": str(ex)[:200]}
     if RANK == 0:
         print(json.dumps(line))
     if dist:
