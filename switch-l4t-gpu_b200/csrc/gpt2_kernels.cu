@@ -397,41 +397,41 @@ extern "C" __global__ void gpt2_lmhead(const float *__restrict__ wte, const floa
 // element-wise steps, causal attention per (token, head).  Only the KV cache
 // is produced (prompt tokens need no logits).
 
-// X[t] = wte[tokens[pos0 + t]] + wpe[pos0 + t] (gpt2_engine.c:178-180).  grid T, block 256.
+// X[t] = wte[tokens[pos0 + t]] + wpe[pos0 + t] (gpt2_engine.c:178-180).  grid (T, any), block 256.
 extern "C" __global__ void gpt2_pf_embed(const float *__restrict__ wte, const float *__restrict__ wpe,
                                          const int *__restrict__ tokens, float *__restrict__ X, int pos0, int C) {
     const int t = blockIdx.x, tok = tokens[pos0 + t];
-    for (int i = threadIdx.x; i < C; i += blockDim.x)
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < C; i += gridDim.y * blockDim.x)
         X[(size_t)t * C + i] = __fadd_rn(wte[(size_t)tok * C + i], wpe[(size_t)(pos0 + t) * C + i]);
 }
 
 // q, k, v of token t = Y[t] + bias; q -> Q[t], k and v -> the cache rows at
-// pos0 + t.  grid T, block 256.
+// pos0 + t.  grid (T, any), block 256.
 extern "C" __global__ void gpt2_pf_qkv(const float *__restrict__ Y, const float *__restrict__ b,
                                        float *__restrict__ Q, float *__restrict__ kc, float *__restrict__ vc, int pos0,
                                        int C) {
     const int t = blockIdx.x, pos = pos0 + t;
     const float *y = Y + (size_t)t * 3 * C;
-    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < C; i += gridDim.y * blockDim.x) {
         Q[(size_t)t * C + i] = __fadd_rn(y[i], b[i]);
         kc[(size_t)pos * C + i] = __fadd_rn(y[C + i], b[C + i]);
         vc[(size_t)pos * C + i] = __fadd_rn(y[2 * C + i], b[2 * C + i]);
     }
 }
 
-// X[t] += Y[t] + bias (gemv_warp_b then add2).  grid T, block 256.
+// X[t] += Y[t] + bias (gemv_warp_b then add2).  grid (T, any), block 256.
 extern "C" __global__ void gpt2_pf_bias_resid(const float *__restrict__ Y, const float *__restrict__ b,
                                               float *__restrict__ X, int n) {
     const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < n; i += gridDim.y * blockDim.x)
         X[(size_t)t * n + i] = __fadd_rn(X[(size_t)t * n + i], __fadd_rn(Y[(size_t)t * n + i], b[i]));
 }
 
-// A[t] = gelu(Y[t] + bias) (gemv_warp_b then gelu).  grid T, block 256.
+// A[t] = gelu(Y[t] + bias) (gemv_warp_b then gelu).  grid (T, any), block 256.
 extern "C" __global__ void gpt2_pf_bias_gelu(const float *__restrict__ Y, const float *__restrict__ b,
                                              float *__restrict__ A, int n) {
     const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < n; i += gridDim.y * blockDim.x)
         A[(size_t)t * n + i] = gelu_ref(__fadd_rn(Y[(size_t)t * n + i], b[i]));
 }
 

@@ -453,11 +453,11 @@ SB_DEV void pf_split(float v, unsigned short *hi, unsigned short *lo) {
     *lo = __half_as_ushort(__float2half_rn(v - __half2float(h)));
 }
 
-// X[t][:] = embedding row of tokens[pos0 + t].  grid T, block 256.
+// X[t][:] = embedding row of tokens[pos0 + t].  grid (T, any), block 256.
 extern "C" __global__ void qwen_pf_embed(const unsigned short *__restrict__ emb, const int *__restrict__ tokens,
                                          float *__restrict__ X, int pos0, int C) {
     const int t = blockIdx.x, tok = tokens[pos0 + t];
-    for (int i = threadIdx.x; i < C; i += blockDim.x) X[(size_t)t * C + i] = h2f_ftz(emb[(size_t)tok * C + i]);
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < C; i += gridDim.y * blockDim.x) X[(size_t)t * C + i] = h2f_ftz(emb[(size_t)tok * C + i]);
 }
 
 // XH rows t (hi) and T + t (lo) = split(RMSNorm(X[t]) * g).  grid T, block 256.
@@ -474,16 +474,16 @@ extern "C" __global__ void qwen_pf_rms_split(const float *__restrict__ X, const 
         pf_split(__fmul_rn(__fmul_rn(x[i], inv), h2f_ftz(g[i])), XH + (size_t)t * C + i, XH + (size_t)(T + t) * C + i);
 }
 
-// XH rows t / T + t = split(X[t]).  grid T, block 256.
+// XH rows t / T + t = split(X[t]).  grid (T, any), block 256.
 extern "C" __global__ void qwen_pf_split(const float *__restrict__ X, unsigned short *__restrict__ XH, int T, int n) {
     const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < n; i += gridDim.y * blockDim.x)
         pf_split(X[(size_t)t * n + i], XH + (size_t)t * n + i, XH + (size_t)(T + t) * n + i);
 }
 
 // QKV of token t = Y[t] + Y[T + t] + bias, RoPE (pairs i, i + HD/2) at
 // pos0 + t for the q and k heads; q -> Q[t], k and v -> the cache rows.
-// grid T, block 256.
+// grid (T, any), block 256.
 extern "C" __global__ void qwen_pf_qkv(const float *__restrict__ Y, const unsigned short *__restrict__ bqkv,
                                        const float *__restrict__ cosT, const float *__restrict__ sinT,
                                        float *__restrict__ Q, float *__restrict__ kc, float *__restrict__ vc, int T,
@@ -491,7 +491,7 @@ extern "C" __global__ void qwen_pf_qkv(const float *__restrict__ Y, const unsign
     const int t = blockIdx.x, pos = pos0 + t;
     const int KVD = NKV * HD, NQKV = C + 2 * KVD, hd2 = HD / 2;
     const float *yh = Y + (size_t)t * NQKV, *yl = Y + (size_t)(T + t) * NQKV;
-    for (int p = threadIdx.x; p < NQKV / 2; p += blockDim.x) {
+    for (int p = blockIdx.y * blockDim.x + threadIdx.x; p < NQKV / 2; p += gridDim.y * blockDim.x) {
         const int h = p / hd2, i = p % hd2, r0 = h * HD + i, r1 = r0 + hd2;
         float y0 = __fadd_rn(__fadd_rn(yh[r0], yl[r0]), h2f_ftz(bqkv[r0]));
         float y1 = __fadd_rn(__fadd_rn(yh[r1], yl[r1]), h2f_ftz(bqkv[r1]));
@@ -556,20 +556,20 @@ extern "C" __global__ void qwen_pf_attn(const float *__restrict__ Q, const float
     }
 }
 
-// X[t] += Y[t] + Y[T + t] (the residual add of a product).  grid T, block 256.
+// X[t] += Y[t] + Y[T + t] (the residual add of a product).  grid (T, any), block 256.
 extern "C" __global__ void qwen_pf_resid(const float *__restrict__ Y, float *__restrict__ X, int T, int n) {
     const int t = blockIdx.x;
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < n; i += gridDim.y * blockDim.x)
         X[(size_t)t * n + i] = __fadd_rn(X[(size_t)t * n + i], __fadd_rn(Y[(size_t)t * n + i], Y[(size_t)(T + t) * n + i]));
 }
 
 // hid = silu(gate) * up from the gate|up product Y (rows of 2*FC), split into
-// hi/lo rows of XH for the down projection.  grid T, block 256.
+// hi/lo rows of XH for the down projection.  grid (T, any), block 256.
 extern "C" __global__ void qwen_pf_swiglu_split(const float *__restrict__ Y, unsigned short *__restrict__ XH, int T,
                                                 int FC) {
     const int t = blockIdx.x;
     const float *yh = Y + (size_t)t * 2 * FC, *yl = Y + (size_t)(T + t) * 2 * FC;
-    for (int i = threadIdx.x; i < FC; i += blockDim.x) {
+    for (int i = blockIdx.y * blockDim.x + threadIdx.x; i < FC; i += gridDim.y * blockDim.x) {
         const float gt = __fadd_rn(yh[i], yl[i]), up = __fadd_rn(yh[FC + i], yl[FC + i]);
         pf_split(__fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), XH + (size_t)t * FC + i,
                  XH + (size_t)(T + t) * FC + i);

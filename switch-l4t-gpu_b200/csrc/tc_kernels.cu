@@ -244,7 +244,10 @@ extern "C" __global__ void gemm_splitk_reduce(const float *__restrict__ ws, floa
 //     promote finished accumulators into FP32 registers, and store C;
 //     warp 1 lane 0 issues tcgen05.mma kind::tf32 (M=128, N=128, K=8);
 //   * M, N arbitrary (TMA zero-fills outside), K % 4 == 0 (16-byte TMA
-//     strides) and N % 4 == 0 (vector stores).
+//     strides) and N % 4 == 0 (vector stores);
+//   * with fewer tiles than SMs (short M, e.g. a prompt prefill) the K range
+//     is split over `splits` CTAs per tile; each writes its partial tile to
+//     ws[split][M][N] and gemm_splitk_reduce adds them in split order.
 namespace t3 {
 constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3, THREADS = 192;
 // The tensor pipe's FP32 accumulation is not IEEE-rounded and its error
@@ -277,11 +280,12 @@ SB_DEV void mbar_arrive(uint64_t *mb) {
 }
 }  // namespace t3
 
-// grid: ceil(M/128) * ceil(N/128) CTAs (blockIdx.x = tile_m * tiles_n + tile_n);
-// block t3::THREADS; dynamic smem: 1024 + STAGES * STAGE + 256 bytes.
+// grid: ceil(M/128) * ceil(N/128) * splits CTAs (blockIdx.x = (tile_m *
+// tiles_n + tile_n) * splits + split); block t3::THREADS; dynamic smem:
+// 1024 + STAGES * STAGE + 256 bytes.  splits == 1: C; else ws[split][M][N].
 extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
     sgemm_3xtf32_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_bt,
-                    float *__restrict__ C, int M, int N, int K) {
+                    float *__restrict__ C, int M, int N, int K, float *__restrict__ ws, int splits) {
     using namespace t3;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -292,8 +296,11 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + NACC);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_n = (N + BN - 1) / BN;
-    const int m0 = (blockIdx.x / tiles_n) * BM, n0 = (blockIdx.x % tiles_n) * BN;
-    const int nk = (K + BK - 1) / BK;
+    const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
+    const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+    const int nk_all = (K + BK - 1) / BK;
+    const int kt0 = (int)((long)nk_all * split / splits);
+    const int nk = (int)((long)nk_all * (split + 1) / splits) - kt0;  // k-slices of this CTA
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -326,8 +333,8 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
                 if (kt >= STAGES && !tck::mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1)) break;
                 unsigned char *st = smem + (size_t)s * STAGE;
                 tck::mbar_expect_tx(&full[s], 2 * TILE);
-                tck::tma_2d(st, &tm_a, kt * BK, m0, &full[s]);
-                tck::tma_2d(st + TILE, &tm_bt, kt * BK, n0, &full[s]);
+                tck::tma_2d(st, &tm_a, (kt0 + kt) * BK, m0, &full[s]);
+                tck::tma_2d(st + TILE, &tm_bt, (kt0 + kt) * BK, n0, &full[s]);
             }
             for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
                 tck::mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
@@ -411,7 +418,7 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
         while (ok && promoted < nchunks) promote(promoted++);
         const int row = m0 + quarter * 32 + lane;
         if (ok && row < M) {
-            float *crow = C + (size_t)row * N + n0;
+            float *crow = (splits == 1 ? C : ws + (size_t)split * M * N) + (size_t)row * N + n0;
             if (n0 + BN <= N) {
 #pragma unroll
                 for (int j = 0; j < BN; j += 4) *reinterpret_cast<float4 *>(crow + j) = make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);

@@ -544,6 +544,8 @@ int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out) {
 
 /* ------------------------------------------------------------------ prefill */
 #define PF_T 128 /* prompt tokens per batch: 2 * PF_T hi/lo rows <= the GEMM's 256 */
+/* element-wise prefill kernels: blocks per token row of n elements (256 threads each) */
+#define PF_GY(n) ((unsigned)CEIL_DIV((n), 256))
 
 /* GPT-2: LayerNorm rows -> 3xTF32 tensor-core products against the [out][in]
  * weights (FP32 accuracy) -> bias / GELU / residual kernels; causal attention
@@ -566,7 +568,7 @@ static int prefill_gpt2(sb_engine *e, int n) {
     for (int p0 = 0; p0 < n; p0 += PF_T) {
         int T = n - p0 < PF_T ? n - p0 : PF_T;
         void *ea[] = {(void *)&wte, (void *)&wpe, &e->tokens, &e->pf_x, &p0, &C};
-        int rc = sb_launch(c, F_G2PF_EMBED, (unsigned)T, 1, 256, 0, s, ea, 0);
+        int rc = sb_launch(c, F_G2PF_EMBED, (unsigned)T, PF_GY(G2_C), 256, 0, s, ea, 0);
         for (int l = 0; !rc && l < G2_NL; l++) {
             const CUdeviceptr lb = e->w + (G2_LBASE + (size_t)l * G2_LAYER) * 4;
             CUdeviceptr ln1w = lb + G2L_LN1W * 4, ln1b = lb + G2L_LN1B * 4, wqkv = lb + G2L_QKVW * 4;
@@ -579,21 +581,21 @@ static int prefill_gpt2(sb_engine *e, int n) {
             rc = sb_launch(c, F_G2_LAYERNORM_ROWS, (unsigned)T, 1, 256, 0, s, la, 0);
             if (!rc) rc = sb_sgemm_nt_3xtf32(pa, (const float *)(uintptr_t)wqkv, py, T, 3 * C, C, s);
             void *qa[] = {&e->pf_y, &bqkv, &e->pf_q, &kc, &vc, &p0, &C};
-            if (!rc) rc = sb_launch(c, F_G2PF_QKV, (unsigned)T, 1, 256, 0, s, qa, 0);
+            if (!rc) rc = sb_launch(c, F_G2PF_QKV, (unsigned)T, PF_GY(G2_C), 256, 0, s, qa, 0);
             if (l == G2_NL - 1) break; /* the last layer's output feeds only logits */
             void *aa[] = {&e->pf_q, &kc, &vc, &e->pf_att, &p0, &C, &NH, &NH, &HD, &scale};
             if (!rc) rc = sb_launch(c, F_PF_ATTN, (unsigned)T, (unsigned)NH, 128, (unsigned)(p0 + T) * 4, s, aa, 0);
             if (!rc) rc = sb_sgemm_nt_3xtf32(patt, (const float *)(uintptr_t)wo, py, T, C, C, s);
             void *ra[] = {&e->pf_y, &bo, &e->pf_x, &C};
-            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_RESID, (unsigned)T, 1, 256, 0, s, ra, 0);
+            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_RESID, (unsigned)T, PF_GY(G2_C), 256, 0, s, ra, 0);
             void *l2[] = {&e->pf_x, &ln2w, &ln2b, &e->pf_a, &C, &eps};
             if (!rc) rc = sb_launch(c, F_G2_LAYERNORM_ROWS, (unsigned)T, 1, 256, 0, s, l2, 0);
             if (!rc) rc = sb_sgemm_nt_3xtf32(pa, (const float *)(uintptr_t)wfc, py, T, FC, C, s);
             void *ga[] = {&e->pf_y, &bfc, &e->pf_a, &FC};
-            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_GELU, (unsigned)T, 1, 256, 0, s, ga, 0);
+            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_GELU, (unsigned)T, PF_GY(G2_FC), 256, 0, s, ga, 0);
             if (!rc) rc = sb_sgemm_nt_3xtf32(pa, (const float *)(uintptr_t)wp, py, T, C, FC, s);
             void *pr[] = {&e->pf_y, &bp, &e->pf_x, &C};
-            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_RESID, (unsigned)T, 1, 256, 0, s, pr, 0);
+            if (!rc) rc = sb_launch(c, F_G2PF_BIAS_RESID, (unsigned)T, PF_GY(G2_C), 256, 0, s, pr, 0);
         }
         if (rc) return rc;
     }
@@ -624,7 +626,7 @@ int sb_engine_prefill(sb_engine *e, int n) {
     for (int p0 = 0; p0 < n; p0 += PF_T) {
         int T = n - p0 < PF_T ? n - p0 : PF_T;
         void *ea[] = {&e->w, &e->tokens, &e->pf_x, &p0, &C};
-        int rc = sb_launch(c, F_PF_EMBED, (unsigned)T, 1, 256, 0, s, ea, 0);
+        int rc = sb_launch(c, F_PF_EMBED, (unsigned)T, PF_GY(QW_C), 256, 0, s, ea, 0);
         for (int l = 0; !rc && l < QW_NL; l++) {
             const CUdeviceptr L = e->w + QW_LBASE + (size_t)l * QW_LSTRIDE;
             CUdeviceptr g_in = L, wqkv = L + QW_C * 2, bqkv = wqkv + (size_t)QW_QKV * QW_C * 2;
@@ -638,24 +640,24 @@ int sb_engine_prefill(sb_engine *e, int n) {
             rc = sb_launch(c, F_PF_RMS_SPLIT, (unsigned)T, 1, 256, 0, s, ra, 0);
             if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wqkv, xh, y, C, QW_QKV, twoT, s);
             void *qa[] = {&e->pf_y, &bqkv, (void *)&cosT, (void *)&sinT, &e->pf_q, &kc, &vc, &T, &p0, &C, &NH, &NKV, &HD};
-            if (!rc) rc = sb_launch(c, F_PF_QKV, (unsigned)T, 1, 256, 0, s, qa, 0);
+            if (!rc) rc = sb_launch(c, F_PF_QKV, (unsigned)T, PF_GY(QW_QKV / 2), 256, 0, s, qa, 0);
             if (l == QW_NL - 1) break; /* the last layer's output feeds only logits */
             /* causal attention, O projection + residual */
             void *aa[] = {&e->pf_q, &kc, &vc, &e->pf_att, &p0, &C, &NH, &NKV, &HD, &scale};
             if (!rc) rc = sb_launch(c, F_PF_ATTN, (unsigned)T, (unsigned)NH, 128, (unsigned)(p0 + T) * 4, s, aa, 0);
             void *sa[] = {&e->pf_att, &e->pf_xh, &T, &C};
-            if (!rc) rc = sb_launch(c, F_PF_SPLIT, (unsigned)T, 1, 256, 0, s, sa, 0);
+            if (!rc) rc = sb_launch(c, F_PF_SPLIT, (unsigned)T, PF_GY(QW_C), 256, 0, s, sa, 0);
             if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wo, xh, y, C, QW_C, twoT, s);
             void *xa[] = {&e->pf_y, &e->pf_x, &T, &C};
-            if (!rc) rc = sb_launch(c, F_PF_RESID, (unsigned)T, 1, 256, 0, s, xa, 0);
+            if (!rc) rc = sb_launch(c, F_PF_RESID, (unsigned)T, PF_GY(QW_C), 256, 0, s, xa, 0);
             /* MLP: RMSNorm -> gate|up -> SwiGLU -> down + residual */
             void *pa[] = {&e->pf_x, &g_post, &e->pf_xh, &T, &C, &eps};
             if (!rc) rc = sb_launch(c, F_PF_RMS_SPLIT, (unsigned)T, 1, 256, 0, s, pa, 0);
             if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wgu, xh, y, C, 2 * QW_FC, twoT, s);
             void *wa[] = {&e->pf_y, &e->pf_xh, &T, &FC};
-            if (!rc) rc = sb_launch(c, F_PF_SWIGLU_SPLIT, (unsigned)T, 1, 256, 0, s, wa, 0);
+            if (!rc) rc = sb_launch(c, F_PF_SWIGLU_SPLIT, (unsigned)T, PF_GY(QW_FC), 256, 0, s, wa, 0);
             if (!rc) rc = sb_gemm_hh((const uint16_t *)(uintptr_t)wdown, xh, y, FC, QW_C, twoT, s);
-            if (!rc) rc = sb_launch(c, F_PF_RESID, (unsigned)T, 1, 256, 0, s, xa, 0);
+            if (!rc) rc = sb_launch(c, F_PF_RESID, (unsigned)T, PF_GY(QW_C), 256, 0, s, xa, 0);
         }
         if (rc) return rc;
     }

@@ -252,10 +252,35 @@ static int sgemm3x_launch(sb_ctx *c, const float *A, const float *Bt, float *C, 
     if (!rc) rc = encode_kmajor_f32(&tb, Bt, K, N);
     if (rc) return rc;
     const long tiles = (long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128);
-    CUdeviceptr cc = DP(C);
-    void *args[] = {&ta, &tb, &cc, &M, &N, &K};
+    /* short or narrow products (a prompt prefill) leave SMs idle: split K
+     * over several CTAs per tile, partial tiles summed in split order */
+    const int nk = CEIL_DIV(K, 32);
+    int splits = 1;
+    if (tiles < c->sms) {
+        splits = (int)CEIL_DIV(c->sms, tiles);
+        if (splits > nk / 2) splits = nk / 2 > 0 ? nk / 2 : 1; /* >= 2 k-slices per CTA */
+    }
+    CUdeviceptr cc = DP(C), ws = 0;
+    if (splits > 1) {
+        const size_t need = (size_t)splits * M * N * 4;
+        if (c->tc_ws_bytes < need) {
+            if (c->tc_ws) cuMemFree(c->tc_ws);
+            c->tc_ws = 0;
+            c->tc_ws_bytes = 0;
+            SB_CK(cuMemAlloc(&c->tc_ws, need));
+            c->tc_ws_bytes = need;
+        }
+        ws = c->tc_ws;
+    }
+    void *args[] = {&ta, &tb, &cc, &M, &N, &K, &ws, &splits};
     const unsigned smem = 1024 + 3 * 65536 + 256;
-    return sb_launch(c, F_SGEMM_3XTF32, (unsigned)tiles, 1, 192, smem, (CUstream)stream, args, 0);
+    rc = sb_launch(c, F_SGEMM_3XTF32, (unsigned)(tiles * splits), 1, 192, smem, (CUstream)stream, args, 0);
+    if (rc || splits == 1) return rc;
+    long total = (long)M * N;
+    void *rargs[] = {&ws, &cc, &total, &splits};
+    long g = CEIL_DIV(total, 256);
+    if (g > 8L * c->sms) g = 8L * c->sms;
+    return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
 }
 
 int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream) {
@@ -266,7 +291,7 @@ int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int 
     if (!c) return SB_ERR_STATE;
     if (M == 0 || N == 0) return 0;
     const long tiles = (long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128);
-    SB_ARG(tiles < 0x7fffffffL, "sgemm_3xtf32: too many tiles");
+    SB_ARG(tiles < 0x7fffffffL / 148, "sgemm_3xtf32: too many tiles");
     /* Bt = B^T (K-major) in a library-owned workspace, grown on demand */
     const size_t need = (size_t)K * N * 4;
     if (c->tc_bt_bytes < need) {
@@ -291,7 +316,7 @@ int sb_sgemm_nt_3xtf32(const float *A, const float *Bt, float *C, int M, int N, 
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     if (M == 0 || N == 0) return 0;
-    SB_ARG((long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128) < 0x7fffffffL, "sgemm_nt_3xtf32: too many tiles");
+    SB_ARG((long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128) < 0x7fffffffL / 148, "sgemm_nt_3xtf32: too many tiles");
     return sgemm3x_launch(c, A, Bt, C, M, N, K, stream);
 }
 

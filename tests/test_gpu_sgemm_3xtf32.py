@@ -1,7 +1,8 @@
 """Opt-in 3xTF32 tensor-core SGEMM against the oracle's restatement of the
 harness loop (gpu_workload.c:97-98): the FP32 bar, relative Frobenius error
 <= 1e-5, plus a Freivalds check of whole products; edge tiles (M, N not
-multiples of 128, K not a multiple of 32) included."""
+multiples of 128, K not a multiple of 32) and split-K launches (fewer tiles
+than SMs) included."""
 import numpy as np
 import pytest
 
@@ -19,7 +20,9 @@ def _mats(M, N, K, seed):
     return A, B
 
 
-@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (1000, 384, 1004), (257, 132, 68), (128, 128, 32)])
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (1000, 384, 1004), (257, 132, 68), (128, 128, 32),
+                                   # prompt-prefill shapes: fewer tiles than SMs, K split over CTAs
+                                   (15, 2304, 768), (15, 768, 3072), (140, 3072, 768), (1, 768, 768)])
 def test_3xtf32_matches_oracle(cuda_dev, M, N, K):
     import torch
     A, B = _mats(M, N, K, 40 + M)
