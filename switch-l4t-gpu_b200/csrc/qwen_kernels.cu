@@ -172,22 +172,20 @@ extern "C" __global__ void __launch_bounds__(256) gemv_h_b200(const unsigned sho
 }
 
 // Y[b][n] = sum_k h2f(W[n][k]) h2f(X[b][k]) for B activation rows (fp16,
-// decoded with the same flush-to-zero rule), FP32 out.  dynamic smem
-// B*K*4.  K % 8 == 0.
+// decoded with the same flush-to-zero rule), FP32 out, on sm_100's
+// mixed-precision FMA (each step equal to fmaf on the decoded values, in the
+// same order).  dynamic smem >= B*K*2.  K % 8 == 0.
 template <int B>
 __device__ void gemv_hh_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
                              float *__restrict__ Y, int K, int N) {
-    extern __shared__ float4 xsb[];
+    extern __shared__ uint4 xhb[];
     constexpr int R = 4;
     int t0, t1;
     cta_task_range((N + R - 1) / R, t0, t1);
     const int cpr = K / 8;
-    float4 *lo = xsb, *hi = xsb + B * cpr;
     for (int i = threadIdx.x; i < B * cpr; i += blockDim.x) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(X + (size_t)i * 8);
-        const float2 f0 = h2x2_ftz(w.x), f1 = h2x2_ftz(w.y), f2 = h2x2_ftz(w.z), f3 = h2x2_ftz(w.w);
-        lo[i] = make_float4(f0.x, f0.y, f1.x, f1.y);
-        hi[i] = make_float4(f2.x, f2.y, f3.x, f3.y);
+        const uint4 v = *reinterpret_cast<const uint4 *>(X + (size_t)i * 8);
+        xhb[i] = make_uint4(ftz_half2_bits(v.x), ftz_half2_bits(v.y), ftz_half2_bits(v.z), ftz_half2_bits(v.w));
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, lane = threadIdx.x & 31;
@@ -195,7 +193,7 @@ __device__ void gemv_hh_body(const unsigned short *__restrict__ W, const unsigne
         int rows[R];
         consecutive_rows<R>(t * R, N, rows);
         float acc[R][B];
-        warp_dot_hb<R, (B > 2 ? 2 : 4), B>(reinterpret_cast<const uint4 *>(W), cpr, rows, cpr, lo, hi, acc);
+        warp_dot_hh<R, (B > 2 ? 2 : 4), B>(reinterpret_cast<const uint4 *>(W), cpr, rows, cpr, xhb, acc);
 #pragma unroll
         for (int r = 0; r < R; r++)
 #pragma unroll

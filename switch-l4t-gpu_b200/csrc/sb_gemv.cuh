@@ -59,6 +59,30 @@ SB_DEV float dot_chunk(WH, const uint4 &w, const float4 &a, const float4 &b, flo
     acc = fmaf(f3.y, b.w, acc);
     return acc;
 }
+// fp16 weights x fp16 activations, FP32 accumulation, with sm_100's
+// mixed-precision FMA (fma.rn.f32.f16: the f16 x f16 product is exact and
+// the sum is rounded once, so each step equals fmaf on the decoded values)
+// -- no fp16 -> fp32 conversions, which bound the CUDA-core dot otherwise.
+// The weight halves are flushed to zero first (mul.ftz by 1.0: subnormals
+// -> 0, normals exact), the reference's h2f rule; x is staged pre-flushed.
+SB_DEV float fma_hh(float acc, unsigned short a, unsigned short b) {
+    asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(acc) : "h"(a), "h"(b));
+    return acc;
+}
+SB_DEV unsigned ftz_h2(unsigned w) {
+    unsigned r;
+    asm("mul.rn.ftz.f16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(0x3C003C00u));
+    return r;
+}
+SB_DEV float dot_chunk_hh(const uint4 &w, const uint4 &x, float acc) {
+    const unsigned ws[4] = {ftz_h2(w.x), ftz_h2(w.y), ftz_h2(w.z), ftz_h2(w.w)}, xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        acc = fma_hh(acc, (unsigned short)(ws[j] & 0xffffu), (unsigned short)(xs[j] & 0xffffu));
+        acc = fma_hh(acc, (unsigned short)(ws[j] >> 16), (unsigned short)(xs[j] >> 16));
+    }
+    return acc;
+}
 SB_DEV float dot_chunk(WF, const uint4 &w, const float4 &a, float acc) {
     acc = fmaf(__uint_as_float(w.x), a.x, acc);
     acc = fmaf(__uint_as_float(w.y), a.y, acc);
@@ -207,6 +231,46 @@ SB_DEV float block_rms_scale(const float *x, int n, float eps, float *red) {
 
 // Batched variant for B activation vectors (FP16 weights): x planes for
 // batch b start at lo + b*(K/8), hi + b*(K/8).  acc[r][b].
+// R rows x B fp16 activation rows (x: B * cpr flushed 16-byte chunks in
+// shared memory), mixed-precision FMAs; warp-reduced sums in acc[][].
+template <int R, int U, int B>
+SB_DEV void warp_dot_hh(const uint4 *W, long ld_chunks, const int (&rows)[R], int cpr, const uint4 *xh,
+                        float (&acc)[R][B]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int b = 0; b < B; b++) acc[r][b] = 0.0f;
+    for (int c0 = lane; c0 < cpr; c0 += 32 * U) {
+        uint4 w[U][R];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = c0 + 32 * u;
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                if (c < cpr && rows[r] >= 0) w[u][r] = ld_stream_u4(W + (long)rows[r] * ld_chunks + c);
+                else w[u][r] = make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = c0 + 32 * u;
+            if (c < cpr) {
+#pragma unroll
+                for (int b = 0; b < B; b++) {
+                    const uint4 x = xh[b * cpr + c];
+#pragma unroll
+                    for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh(w[u][r], x, acc[r][b]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int b = 0; b < B; b++) acc[r][b] = warp_sum(acc[r][b]);
+}
+
 template <int R, int U, int B>
 SB_DEV void warp_dot_hb(const uint4 *W, long ld_chunks, const int (&rows)[R], int cpr, const float4 *lo,
                         const float4 *hi, float (&acc)[R][B]) {
