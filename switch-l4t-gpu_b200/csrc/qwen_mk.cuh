@@ -98,6 +98,50 @@ SB_DEV void smem_rows_dot(const uint4 *base, int stride, int nvalid, const float
     for (int r = 0; r < R; r++) out[r] = f2_sum(acc[r]);
 }
 
+// The same dot with x given as two fp16 vectors, x = xh + xl (xh = fp16(x),
+// xl = fp16(x - xh): ~22 bits of x), on sm_100's mixed-precision FMA
+// (fma.rn.f32.f16: exact f16 x f16 product, one FP32 rounding), which needs
+// no fp16 -> fp32 conversions -- the limit of the form above.  Two FP32
+// accumulators per row (xh terms, xl terms).  Used where x is a norm or an
+// attention output (|x| far below the fp16 range), not for the MLP hidden
+// vector.  Weights are pre-flushed, so no subnormal handling here.
+SB_DEV float fma_hh(float acc, unsigned short a, unsigned short b) {
+    asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(acc) : "h"(a), "h"(b));
+    return acc;
+}
+template <int R>
+SB_DEV void smem_rows_dot_hl(const uint4 *base, int stride, int nvalid, const uint4 *xh, const uint4 *xl, int c0,
+                             int c1, int row_c0, float (&out)[R]) {
+    float ah[R], al[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) ah[r] = al[r] = 0.f;
+    for (int c = c0 + (threadIdx.x & 31); c < c1; c += 32) {
+        const uint4 h = xh[c], l = xl[c];
+        const unsigned hs[4] = {h.x, h.y, h.z, h.w}, ls[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            if (r < nvalid) {
+                const uint4 w = base[r * stride + c - row_c0];
+                const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const unsigned short w0 = ws[j] & 0xffffu, w1 = ws[j] >> 16;
+                    ah[r] = fma_hh(ah[r], w0, (unsigned short)(hs[j] & 0xffffu));
+                    al[r] = fma_hh(al[r], w0, (unsigned short)(ls[j] & 0xffffu));
+                    ah[r] = fma_hh(ah[r], w1, (unsigned short)(hs[j] >> 16));
+                    al[r] = fma_hh(al[r], w1, (unsigned short)(ls[j] >> 16));
+                }
+            }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) out[r] = ah[r] + al[r];
+}
+SB_DEV void split_hl(float v, unsigned short &h, unsigned short &l) {
+    const __half hv = __float2half_rn(v);
+    h = __half_as_ushort(hv);
+    l = __half_as_ushort(__float2half_rn(v - __half2float(hv)));
+}
+
 // Element i of a K-vector lives in plane (i%8)<4 ? lo : hi, float (i/8)*4 + i%4.
 SB_DEV float *plane_elem(float4 *lo, float4 *hi, int i) {
     return reinterpret_cast<float *>((i & 7) < 4 ? lo : hi) + (i >> 3) * 4 + (i & 3);
@@ -106,7 +150,7 @@ SB_DEV float *plane_elem(float4 *lo, float4 *hi, int i) {
 // RMSNorm from registers: thread t < C/2 holds elements (2t, 2t+1) of x in
 // xv and the two fp16 gains in gw (packed); writes x*inv*g into the split
 // planes.
-SB_DEV void rms_regs(float2 xv, unsigned gw, float4 *lo, float4 *hi, float *red, float eps) {
+SB_DEV void rms_regs(float2 xv, unsigned gw, unsigned *xh, unsigned *xl, float *red, float eps) {
     const int t = threadIdx.x;
     const bool act = t < C / 2;
     float s = act ? fmaf(xv.x, xv.x, xv.y * xv.y) : 0.0f;
@@ -114,8 +158,11 @@ SB_DEV void rms_regs(float2 xv, unsigned gw, float4 *lo, float4 *hi, float *red,
     const float inv = 1.0f / sqrtf(__fdiv_rn(s, (float)C) + eps);
     if (act) {
         const float g0 = h2f_ftz((unsigned short)(gw & 0xffffu)), g1 = h2f_ftz((unsigned short)(gw >> 16));
-        const float2 y = make_float2(__fmul_rn(__fmul_rn(xv.x, inv), g0), __fmul_rn(__fmul_rn(xv.y, inv), g1));
-        *reinterpret_cast<float2 *>(plane_elem(lo, hi, 2 * t)) = y;
+        unsigned short h0, l0, h1, l1;
+        split_hl(__fmul_rn(__fmul_rn(xv.x, inv), g0), h0, l0);
+        split_hl(__fmul_rn(__fmul_rn(xv.y, inv), g1), h1, l1);
+        xh[t] = h0 | ((unsigned)h1 << 16);  // elements 2t, 2t + 1
+        xl[t] = l0 | ((unsigned)l1 << 16);
     }
 }
 
@@ -123,7 +170,7 @@ SB_DEV void rms_regs(float2 xv, unsigned gw, float4 *lo, float4 *hi, float *red,
 
 // grid: one CTA per SM (cooperative launch, >= 128 CTAs); block qmk::THREADS;
 // dynamic smem: FC*4 + WARPS*WREG + score_cap*4
-//               + (32 + WARPS*64 + WARPS + NH*SPLITS_MAX*2)*4 bytes.
+//               + (32 + WARPS*64 + WARPS + NH*SPLITS_MAX*2)*4 + C*4 bytes.
 extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(const SbMkParams raw) {
     using namespace qmk;
     const Params p(raw);
@@ -138,6 +185,10 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
     float *opart = red + 32;                          // WARPS x HD per-warp partial P.V
     float *ksum = opart + WARPS * HD;                 // WARPS floats: split-K partials / per-warp softmax sums
     float *mlv = ksum + WARPS;                        // NH*SPLITS_MAX (m, l) pairs of the partials
+    // K = C activations as fp16 hi / lo vectors (S1, S3, S4 and LM-head dots)
+    uint4 *xh4 = reinterpret_cast<uint4 *>(mlv + NH * SPLITS_MAX * 2), *xl4 = xh4 + CPR;
+    unsigned *xhw = reinterpret_cast<unsigned *>(xh4), *xlw = reinterpret_cast<unsigned *>(xl4);
+    unsigned short *xhs = reinterpret_cast<unsigned short *>(xh4), *xls = reinterpret_cast<unsigned short *>(xl4);
     __shared__ float wmax_s[WARPS], xown[8], gu_s[96];
     __shared__ unsigned long long best_s;
     __shared__ __align__(8) uint64_t mbar[WARPS][2 + LM_NB];
@@ -321,7 +372,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         // ================= S1: RMSNorm -> QKV -> RoPE -> q, k, v words
         if (l > 0 && !wait_x(epoch(l - 1, 4))) { aborted = true; break; }
         stamp(l, 0, 0);
-        rms_regs(xv, gw1, xlo, xhi, red, eps);
+        rms_regs(xv, gw1, xhw, xlw, red, eps);
         __syncthreads();
         // (An L2 prefetch of the LM-head rows during the last layers measured
         // 10 us per token slower: it competes with those layers' weights.)
@@ -332,7 +383,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             const int h = pp1 / 32, i = pp1 % 32;
             const int r0 = h * HD + i, r1 = r0 + 32;
             float a[2];
-            smem_rows_dot<2>(wreg4, CPR, 2, xlo, xhi, 0, CPR, 0, a);
+            smem_rows_dot_hl<2>(wreg4, CPR, 2, xh4, xl4, 0, CPR, 0, a);
             const float a0 = warp_sum(a[0]), a1 = warp_sum(a[1]);
             if (lane == 0) {
                 float y0 = __fadd_rn(a0, b0), y1 = __fadd_rn(a1, b1);
@@ -541,7 +592,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                         acc = fmaf(wgt, ov[u][s], acc);
                     }
                 }
-                *plane_elem(xlo, xhi, d) = acc / Lsum;
+                split_hl(acc / Lsum, xhs[d], xls[d]);
             }
         }
         __syncthreads();
@@ -550,7 +601,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         {
             const int r = or0 + warp / 2, half = warp % 2;
             float a[1];
-            smem_rows_dot<1>(wreg4 + WHEAD / 16, 0, r < or1 ? 1 : 0, xlo, xhi, half * (CPR / 2), (half + 1) * (CPR / 2),
+            smem_rows_dot_hl<1>(wreg4 + WHEAD / 16, 0, r < or1 ? 1 : 0, xh4, xl4, half * (CPR / 2), (half + 1) * (CPR / 2),
                              half * (CPR / 2), a);
             resid_update(warp_sum(a[0]), epoch(l, 2));
         }
@@ -560,13 +611,13 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         if (prefetcher) prefetch_piece(l + 1, 3);
         if (!wait_x(epoch(l, 2))) { aborted = true; break; }
         stamp(l, 3, 0);
-        rms_regs(xv, gw4, xlo, xhi, red, eps);
+        rms_regs(xv, gw4, xhw, xlw, red, eps);
         __syncthreads();
         wait_slot(0);
         __syncwarp();
         {
             float a[5];
-            smem_rows_dot<5>(wreg4, CPR, gu_nr, xlo, xhi, 0, CPR, 0, a);
+            smem_rows_dot_hl<5>(wreg4, CPR, gu_nr, xh4, xl4, 0, CPR, 0, a);
 #pragma unroll
             for (int t = 0; t < 5; t++) {
                 const float d = warp_sum(a[t]);
@@ -664,7 +715,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
                     if ((pend >> i) & 1u) mbar_wait(&mb[i], (phase >> i) & 1u);
             return;
         }
-        rms_regs(xv, gwf, xlo, xhi, red, eps);
+        rms_regs(xv, gwf, xhw, xlw, red, eps);
         __syncthreads();
         unsigned long long best = 0ull;
         for (int k = 0; k < ngrp; k++) {
@@ -672,7 +723,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             wait_slot(2 + slot);
             __syncwarp();
             float a[LM_G];
-            smem_rows_dot<LM_G>(wreg4 + slot * LM_G * CPR, CPR, nj, xlo, xhi, 0, CPR, 0, a);
+            smem_rows_dot_hl<LM_G>(wreg4 + slot * LM_G * CPR, CPR, nj, xh4, xl4, 0, CPR, 0, a);
 #pragma unroll
             for (int j = 0; j < LM_G; j++) {
                 const float dotv = warp_sum(a[j]);

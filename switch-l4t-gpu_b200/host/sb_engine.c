@@ -62,10 +62,12 @@ struct sb_engine {
 static unsigned mk_smem_bytes(int model, int score_cap) {
     /* Qwen: x planes (FC floats) | 16 warp regions of (6 rows + 1/2 row) of 896 fp16
      * GPT-2: x (FC floats) | 16 warp regions of (3 rows + 1/2 row) of 768 fp32
-     * both: | scores | red(32) opart(16x64) ksum(16) (m, l) of NH x SPLITS_MAX partials */
+     * both: | scores | red(32) opart(16x64) ksum(16) (m, l) of NH x SPLITS_MAX partials
+     * Qwen: | fp16 hi / lo activation vectors (C halves each) */
     const unsigned head = model == SB_MODEL_QWEN ? QW_FC * 4 + MK_WARPS * (6 * QW_C * 2 + QW_C)
                                                  : G2_FC * 4 + MK_WARPS * (3 * G2_C * 4 + G2_C * 2);
-    return head + (unsigned)score_cap * 4 + (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4;
+    const unsigned hl = model == SB_MODEL_QWEN ? QW_C * 4 : 0; /* fp16 hi / lo activation vectors */
+    return head + (unsigned)score_cap * 4 + (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4 + hl;
 }
 
 /* ------------------------------------------------------------------ upload */
