@@ -191,15 +191,23 @@ void *sb_engine_stream(sb_engine *e);
 int sb_engine_logits(sb_engine *e, const float **dev_logits, int *vocab);
 /* Kernel launches issued per decode step (with / without LM head). */
 int sb_engine_launches_per_step(sb_engine *e, int with_logits);
-/* 1 when the step runs as the persistent whole-step kernel (Qwen on GPUs
- * with >= 128 SMs: one cooperative launch per token, grid-wide barriers
- * between stages), 0 for one kernel per stage. */
+/* 1 when the step runs as the persistent whole-step kernel (GPUs with >= 128
+ * SMs: one cooperative launch per token, stages handed over through flagged
+ * exchange words), 0 for one kernel per stage. */
 int sb_engine_uses_persistent_kernel(sb_engine *e);
-/* Profiling aid for the persistent kernel: dev_buf (u64[SMs][128][2], or
- * NULL to stop) receives %globaltimer stamps at every grid barrier, per
- * CTA: [cta][k][0] = arrival at barrier k, [cta][k][1] = release
- * ([cta][0][0] = kernel start).  Graphs are re-captured on next use. */
+/* Profiling aid for the persistent kernel: dev_buf (u64[SMs][256], or NULL
+ * to stop) receives %globaltimer stamps per CTA: [cta][0] = kernel start,
+ * [cta][1 + 2k] / [cta][2 + 2k] = inputs ready / outputs written of stage
+ * k = layer * 5 + stage.  Graphs are re-captured on next use.  No
+ * counterpart in the reference. */
 int sb_engine_set_trace(sb_engine *e, void *dev_buf);
+/* Failure-detection test hook for the persistent kernel (no counterpart in
+ * the reference): cta >= 0 makes that CTA withhold its layer-0 outputs, so
+ * every other CTA's bounded wait runs out (~1 s), the kernel returns early
+ * and the step reports SB_ERR_STATE ("a wait inside the persistent kernel
+ * timed out"); the engine clears its exchange words and stays usable.  -1
+ * turns it off.  Graphs are re-captured on next use. */
+int sb_engine_set_test_stall(sb_engine *e, int cta);
 /* Bytes of weights a decode step streams (with LM head). */
 double sb_engine_step_bytes(sb_engine *e);
 /* Time `reps` standalone launches (CUDA events on the engine stream) of one

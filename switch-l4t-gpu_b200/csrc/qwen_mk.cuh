@@ -324,7 +324,8 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             const float y = ksum[2 * tid] + ksum[2 * tid + 1];
             const float xn = __fadd_rn(xown[tid], y);
             xown[tid] = xn;
-            ll_put(llx + or0 + tid, xn, e);
+            // test hook: the stalled CTA withholds its layer-0 outputs
+            if (!(p.test_stall == b + 1 && e == epoch(0, 4))) ll_put(llx + or0 + tid, xn, e);
         }
     };
     // x words of epoch e -> xv (thread t < C/2: elements 2t, 2t+1); uniform

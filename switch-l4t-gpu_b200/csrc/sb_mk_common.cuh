@@ -33,11 +33,12 @@ struct Params {
     int with_logits;
     int splits;              // attention T-splits per head (<= SPLITS_MAX)
     int score_cap;           // positions per split the score buffer holds
+    int test_stall;          // test hook (SbMkParams.test_stall)
     SB_DEV explicit Params(const SbMkParams &r)
         : w((const unsigned short *)r.w), kv((float *)r.kv), ll((u64 *)r.ll), logits((float *)r.logits),
           st((SbStep *)r.st), tokens((int *)r.tokens), sync((unsigned *)r.sync), err((int *)r.err),
           trace((unsigned long long *)r.trace), ctx_cap(r.ctx_cap), with_logits(r.with_logits),
-          splits(r.splits), score_cap(r.score_cap) {}
+          splits(r.splits), score_cap(r.score_cap), test_stall(r.test_stall) {}
 };
 
 // ------------------------------------------------------------------ PTX helpers

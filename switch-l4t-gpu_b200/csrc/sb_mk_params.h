@@ -27,6 +27,9 @@ typedef struct SbMkParams {
     int with_logits;
     int splits;                /* attention T-splits per head (<= SPLITS_MAX)    */
     int score_cap;             /* positions one split's score buffer holds       */
+    int test_stall;            /* test hook: 0, or k > 0 -- CTA k-1 withholds its
+                                * layer-0 outputs, so every other CTA's bounded
+                                * wait runs out and the step reports an error */
 } SbMkParams;
 
 #endif

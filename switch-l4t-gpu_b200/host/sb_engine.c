@@ -52,6 +52,7 @@ struct sb_engine {
     unsigned mk_smem;
     long mk_steps; /* launches since the flagged words were last cleared */
     CUdeviceptr trace;
+    int test_stall; /* sb_engine_set_test_stall */
     /* batched prompt prefill: activations of up to PF_T tokens */
     CUdeviceptr pf_x, pf_xh, pf_y, pf_q, pf_att, pf_a;
     SbStep st_begin; /* the step state sb_engine_begin wrote */
@@ -244,6 +245,7 @@ static int record_mk(sb_engine *e, int with_logits) {
     prm.with_logits = with_logits;
     prm.splits = e->mk_splits;
     prm.score_cap = e->mk_score_cap;
+    prm.test_stall = e->test_stall;
     void *args[] = {&prm};
     return sb_launch_coop(e->c, mk_fn(e->model), (unsigned)e->c->sms, MK_THREADS, e->mk_smem, e->stream, args);
 }
@@ -745,6 +747,19 @@ int sb_engine_profile(sb_engine *e, int which, int reps, void *flush, size_t flu
 }
 
 int sb_engine_uses_persistent_kernel(sb_engine *e) { return e && e->mk; }
+
+int sb_engine_set_test_stall(sb_engine *e, int cta) {
+    if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);
+    SB_ARG(e->mk, "the test stall applies to the persistent step kernel only");
+    SB_ARG(cta >= -1 && cta < e->c->sms, "cta out of range");
+    e->test_stall = cta + 1;
+    for (int i = 0; i < 2; i++)
+        if (e->gexec[i]) {
+            cuGraphExecDestroy(e->gexec[i]);
+            e->gexec[i] = NULL;
+        }
+    return 0;
+}
 
 int sb_engine_set_trace(sb_engine *e, void *dev_buf) {
     if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);

@@ -107,6 +107,7 @@ def lib():
     _sig(L.sb_engine_step_bytes, D, P)
     _sig(L.sb_engine_uses_persistent_kernel, I, P)
     _sig(L.sb_engine_set_trace, I, P, P)
+    _sig(L.sb_engine_set_test_stall, I, P, I)
     _sig(L.sb_engine_profile, I, P, I, I, P, ctypes.c_size_t, ctypes.POINTER(F), ctypes.POINTER(D))
     _sig(L.sb_synth_weights, ctypes.c_long, I, ctypes.c_char_p, U64)
     _sig(L.sb_synth_ids, None, P, I, I, U64)
@@ -335,6 +336,11 @@ class Engine:
 
     def set_trace(self, buf):
         check(lib().sb_engine_set_trace(self.h, _p(buf)))
+
+    def set_test_stall(self, cta):
+        """Failure-detection test hook: CTA `cta` withholds its layer-0
+        outputs (-1: off); see sb_engine_set_test_stall."""
+        check(lib().sb_engine_set_test_stall(self.h, cta))
 
     @property
     def persistent(self):

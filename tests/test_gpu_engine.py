@@ -68,6 +68,38 @@ def test_gpt2_default_is_persistent(cuda_dev, gpt2_weights):
 
 
 @pytest.mark.parametrize("model", ["qwen", "gpt2"])
+def test_persistent_wait_timeout_recovers(cuda_dev, qwen_weights, gpt2_weights, model):
+    """Failure detection without a GPU fault: one CTA withholds its layer-0
+    outputs (a word nothing else writes), every other CTA's bounded wait runs
+    out, the kernel returns early and the host reports the timeout; the
+    engine clears its exchange words and then decodes correctly again."""
+    import time
+    mid, w, V = ((sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"]) if model == "qwen"
+                 else (sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"]))
+    eng = sb200.Engine(mid, w, 32)
+    if not eng.persistent:
+        eng.close()
+        pytest.skip("the persistent step kernel needs >= 128 SMs")
+    ref = orc.Model(model, w, 32, V)
+    ids = sb200.synth_ids(3, V, 23)
+    try:
+        got = np.zeros(V, dtype=np.float32)
+        eng.set_test_stall(5)
+        t0 = time.time()
+        with pytest.raises(sb200.SbError, match="timed out"):
+            eng.forward(ids[0], 0, True, got)
+        assert time.time() - t0 < 60
+        eng.set_test_stall(-1)
+        for p, t in enumerate(ids):
+            eng.forward(t, p, True, got)
+            want = ref.forward(t, p, True)
+            assert _rel(got, want) <= LOGIT_TOL, f"pos {p} after recovery: {_rel(got, want):.2e}"
+    finally:
+        eng.close()
+        ref.close()
+
+
+@pytest.mark.parametrize("model", ["qwen", "gpt2"])
 def test_persistent_graph_matches_direct(cuda_dev, qwen_weights, gpt2_weights, model):
     """The persistent kernel replayed from a graph and launched directly give
     bit-identical logits."""
