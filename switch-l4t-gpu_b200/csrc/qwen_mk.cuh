@@ -344,6 +344,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         for (int piece = 0; piece < 5; piece++) prefetch_piece(0, piece);
     fence_async();
     copy_s1(0);
+    copy_s3(0);  // O rows: one layer ahead from here on
     // layer-0 S1 input: the embedding row (constant: nothing to wait for)
     if (xact) {
         const unsigned e2 = *reinterpret_cast<const unsigned *>(emb + (long)tok * C + 2 * tid);
@@ -409,7 +410,6 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
         const bool has_item = b < NH * nsplit;
         auto issue_s3_s4 = [&]() {
             fence_async();
-            copy_s3(l);
             copy_s4_piece(l, 0);
             copy_s4_piece(l, 1);
             if (prefetcher) prefetch_piece(l + 1, 1);
@@ -605,6 +605,10 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk(con
             smem_rows_dot_hl<1>(wreg4 + WHEAD / 16, 0, r < or1 ? 1 : 0, xh4, xl4, half * (CPR / 2), (half + 1) * (CPR / 2),
                              half * (CPR / 2), a);
             resid_update(warp_sum(a[0]), epoch(l, 2));
+        }
+        if (l + 1 < NL) {  // the tail slot is read: the next layer's O rows, a layer
+            fence_async();   // ahead (-3 us per token; for GPT-2 the same measured slower)
+            copy_s3(l + 1);
         }
         stamp(l, 2, 1);
         // ================= S4: RMSNorm -> gate/up -> SwiGLU -> hid words
