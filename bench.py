@@ -435,11 +435,14 @@ def gpt2_section(torch, dev, dist, steps, warmup, with_cpu):
 def gemv_section(torch, dev):
     """Standalone FP16 GEMV sweep y = W.x (fp16 W and x, fp32 y) at batch 1
     (CUDA cores), 4 and 16 (tcgen05 tensor cores); W copies rotated through
-    1 GiB so every launch streams from HBM."""
+    1 GiB so every launch streams from HBM.  The timed launches are replayed
+    from a CUDA graph, so the small shapes measure the kernels, not the
+    per-call Python launch path."""
     import sb200
     peaks = measured_peaks()
     peak = float(peaks["hbm_gbs"]) if peaks and peaks.get("hbm_gbs") else FALLBACK_HBM_GBS
     pool = torch.empty(1 << 29, dtype=torch.float16, device=dev).normal_(0, 0.02)  # 1 GiB
+    side = torch.cuda.Stream(dev)
     out = {}
     for (N, K) in GEMV_SHAPES:
         wsz = N * K
@@ -449,20 +452,30 @@ def gemv_section(torch, dev):
             X = torch.randn(Bw, K, device=dev).half()
             Y = torch.empty(Bw, N, device=dev)
             fn = sb200.gemv_hh if Bw == 1 else sb200.gemm_hh  # batches 4 and 16: tcgen05 tensor cores
-            for i in range(min(ncopy, 4)):
-                fn(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):  # warm-up (workspaces are allocated here, outside the capture)
+                for i in range(min(ncopy, 4)):
+                    fn(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw, stream=side)
+            side.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                cap = torch.cuda.current_stream(dev)
+                for r in range(reps):
+                    i = r % ncopy
+                    fn(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw, stream=cap)
+            graph.replay()  # warm replay
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for r in range(reps):
-                i = r % ncopy
-                fn(pool[i * wsz:(i + 1) * wsz], X, Y, K, N, Bw)
+            graph.replay()
             e1.record()
             e1.synchronize()
+            del graph
             us = e0.elapsed_time(e1) * 1e3 / reps
             nbytes = wsz * 2 + Bw * K * 2 + Bw * N * 4
             gbs = nbytes / (us * 1e-6) / 1e9
             out[f"{N}x{K}_b{Bw}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
-                                     "l2": "rotating copies" if ncopy * wsz * 2 > 4 * 126e6 else "L2-resident"}
+                                     "l2": "rotating copies" if ncopy * wsz * 2 > 4 * 126e6 else "L2-resident",
+                                     "launches": "CUDA-graph replay of %d" % reps}
     del pool
     torch.cuda.empty_cache()
     return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1 (CUDA cores); b4, b16: gemm_hh_tc (tcgen05)",
