@@ -33,7 +33,8 @@
 //   S3 combine partials -> att; O rows; x += O att  -> x words (own rows)
 //   S4 RMSNorm(x) -> gate/up row pairs -> SwiGLU -> hid words
 //   S5 down rows (split-K over warp pairs); x += down hid -> x words
-// then final RMSNorm -> LM head rows (bulk-copy ring per warp) -> logits +
+// then final RMSNorm -> LM head rows (three-row groups per warp, two groups
+// of bulk copies in flight) -> logits +
 // argmax; CTA 0 counts the arrivals and finalises the step (next token,
 // position, sequence number).
 //
