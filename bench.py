@@ -52,7 +52,7 @@ N_PROMPT, N_GEN, MAX_CTX = 32, 256, 2048
 WEIGHT_SEED = 20261201
 METRIC = "Qwen-0.5B-shape FP16 decode tok/s"
 UNIT = "tok/s"
-BASELINE_TOKS = 8.9  # Qwen2.5-0.5B FP16 decode on Tegra X1 (gpu-llm/STATUS.md:112)
+BASELINE_TOKS = 8.9  # the reference's published Qwen2.5-0.5B FP16 decode rate on Tegra X1 (gpu-llm/STATUS.md:112)
 FALLBACK_HBM_GBS = 6650.0
 CPU_SAMPLE_TOKENS = 16  # per host core: about 10 s of reference CPU decode
 CONFIG = {
