@@ -79,9 +79,9 @@ SB_DEV void rows_dot_f32(const float4 *base, int stride, int nvalid, const float
 SB_DEV void ln_regs(float2 xv, const float *w, const float *bias, float *xs, float *red, float eps) {
     const int t = threadIdx.x;
     const bool act = t < C / 2;
-    const float mean = __fdiv_rn(block_sum(act ? xv.x + xv.y : 0.f, red), (float)C);
+    const float mean = __fdiv_rn(block_sum1(act ? xv.x + xv.y : 0.f, red, 0), (float)C);
     const float d0 = xv.x - mean, d1 = xv.y - mean;
-    const float var = __fdiv_rn(block_sum(act ? fmaf(d0, d0, d1 * d1) : 0.f, red), (float)C);
+    const float var = __fdiv_rn(block_sum1(act ? fmaf(d0, d0, d1 * d1) : 0.f, red, 16), (float)C);
     const float inv = 1.0f / sqrtf(var + eps);
     if (act) {
         const float2 g = *reinterpret_cast<const float2 *>(w + 2 * t), bb = *reinterpret_cast<const float2 *>(bias + 2 * t);

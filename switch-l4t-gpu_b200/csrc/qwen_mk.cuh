@@ -155,7 +155,7 @@ SB_DEV void rms_regs(float2 xv, unsigned gw, unsigned *xh, unsigned *xl, float *
     const int t = threadIdx.x;
     const bool act = t < C / 2;
     float s = act ? fmaf(xv.x, xv.x, xv.y * xv.y) : 0.0f;
-    s = block_sum(s, red);
+    s = block_sum1(s, red, 0);
     const float inv = 1.0f / sqrtf(__fdiv_rn(s, (float)C) + eps);
     if (act) {
         const float g0 = h2f_ftz((unsigned short)(gw & 0xffffu)), g1 = h2f_ftz((unsigned short)(gw >> 16));

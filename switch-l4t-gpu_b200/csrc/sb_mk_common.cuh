@@ -125,6 +125,20 @@ SB_DEV bool mbar_wait(uint64_t *mb, unsigned ph) {
     return false;
 }
 
+// Block-wide sum for the step kernels with one barrier: the warp partials go
+// to red[off .. off + 16), and the caller alternates `off` (0 / 16) between
+// consecutive reductions, so a reduction never overwrites partials another
+// warp may still be reading (the stage code between two uses of the same
+// half always passes a barrier).  THREADS = 512 (16 warps).
+SB_DEV float block_sum1(float v, float *red, int off) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) red[off + w] = v;
+    __syncthreads();
+    float s = (lane < 16) ? red[off + lane] : 0.0f;
+    return warp_sum(s);
+}
+
 // Contiguous share [lo, hi) of n units for CTA b of g.
 SB_DEV void share(int n, int b, int g, int &lo, int &hi) {
     lo = (int)((long)n * b / g);
