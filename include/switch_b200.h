@@ -87,7 +87,8 @@ int sb_gemv_multi_f32(const float *W, const float *X, const float *bias, float *
 int sb_gemv_h(const uint16_t *W, const float *x, const float *bias, float *y, int K, int N, void *stream);
 /* FP16 weights and FP16 activations, batch B in 1..8: Y[b][n] =
  * sum_k h2f(W[n][k]) h2f(X[b][k]), FP32 accumulate and output (the GEMV
- * sweep's y = W x with x FP16).  K % 8 == 0. */
+ * sweep's y = W x with x FP16).  K % 8 == 0.  Outputs shorter than 8 rows
+ * per SM run split-K (K divided over a CTA's warps). */
 int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
 /* The same product for B in 1..256 on the 5th-generation tensor cores
  * (tcgen05, TMA-fed, FP32 accumulation in tensor memory): the batched-decode

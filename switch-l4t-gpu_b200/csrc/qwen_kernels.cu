@@ -214,6 +214,87 @@ extern "C" __global__ void __launch_bounds__(256) gemv_hh4(const unsigned short 
     gemv_hh_body<4>(W, X, Y, K, N);
 }
 
+// The same product for short outputs (N = 896 gives 224 four-row tasks:
+// a warp per task would leave most SMs idle with a few KB in flight each).
+// One CTA per four-row task; its 8 warps take contiguous eighths of K, so
+// a CTA keeps 8 warps x 16 row-chunks of 16 B in flight.  x is read from
+// global memory (L1-cached, shared by the CTAs of an SM) and flushed per
+// use, so there is no staging round trip.  Warp partials are added in
+// warp order in shared memory.  Block 256.
+template <int B>
+__device__ void gemv_hh_sk_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
+                                float *__restrict__ Y, int K, int N) {
+    constexpr int R = 4, NW = 8, U = 4;
+    __shared__ float part[NW][R * B];
+    const int cpr = K / 8, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = (cpr + NW - 1) / NW;
+    const int c_lo = min(cpr, warp * per), c_hi = min(cpr, c_lo + per);
+    const uint4 *W4 = reinterpret_cast<const uint4 *>(W);
+    const uint4 *X4 = reinterpret_cast<const uint4 *>(X);
+    for (int t = blockIdx.x; t < (N + R - 1) / R; t += gridDim.x) {
+        int rows[R];
+        consecutive_rows<R>(t * R, N, rows);
+        float acc[R][B];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int b = 0; b < B; b++) acc[r][b] = 0.0f;
+        for (int c0 = c_lo + lane; c0 < c_hi; c0 += 32 * U) {
+            uint4 w[U][R];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int c = c0 + 32 * u;
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    w[u][r] = (c < c_hi && rows[r] >= 0) ? ld_stream_u4(W4 + (long)rows[r] * cpr + c)
+                                                          : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int c = c0 + 32 * u;
+                if (c < c_hi) {
+#pragma unroll
+                    for (int b = 0; b < B; b++) {
+                        const uint4 v = __ldg(X4 + (long)b * cpr + c);
+                        const uint4 x = make_uint4(ftz_half2_bits(v.x), ftz_half2_bits(v.y), ftz_half2_bits(v.z),
+                                                   ftz_half2_bits(v.w));
+#pragma unroll
+                        for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh(w[u][r], x, acc[r][b]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const float v = warp_sum(acc[r][b]);
+                if (lane == 0) part[warp][r * B + b] = v;
+            }
+        __syncthreads();
+        if (threadIdx.x < R * B) {
+            const int r = threadIdx.x / B, b = threadIdx.x % B;
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) s += part[w][threadIdx.x];
+            if (t * R + r < N) Y[(size_t)b * N + t * R + r] = s;
+        }
+        __syncthreads();  // part is reused by the CTA's next task
+    }
+}
+extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk1(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<1>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk2(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<2>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk4(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<4>(W, X, Y, K, N);
+}
+
 // GQA decode attention with an explicit T (no step state); 7 query heads
 // per KV head.  grid (NKV, max_splits), block SB_ATTN_THREADS.
 extern "C" __global__ void attn_decode_g7(const float *__restrict__ q, const float *__restrict__ kc,

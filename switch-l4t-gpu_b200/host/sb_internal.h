@@ -34,6 +34,9 @@ typedef enum {
     F_GEMV_HH1,
     F_GEMV_HH2,
     F_GEMV_HH4,
+    F_GEMV_HH_SK1,
+    F_GEMV_HH_SK2,
+    F_GEMV_HH_SK4,
     F_RMSNORM,
     F_ROPE,
     F_SWIGLU,

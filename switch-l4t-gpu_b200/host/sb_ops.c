@@ -103,14 +103,23 @@ int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     SB_ARG(K % 8 == 0 && ALIGNED16(W) && ALIGNED16(X), "gemv_hh needs K % 8 == 0 and 16-byte aligned W, X");
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
+    /* Fewer four-row tasks than two per SM: the split-K form (a CTA per
+     * task, K split over its warps); else a warp per task. */
+    const long tasks = CEIL_DIV(N, 4);
+    const int split_k = tasks < 2L * c->sms;
     for (int b0 = 0; b0 < B;) {
         int nb = B - b0 >= 4 ? 4 : (B - b0 >= 2 ? 2 : 1);
-        SB_ARG((size_t)nb * K * 4 <= 220 * 1024, "gemv_hh: batch x K too large for the shared x stage");
-        sb_fn_id f = nb == 4 ? F_GEMV_HH4 : (nb == 2 ? F_GEMV_HH2 : F_GEMV_HH1);
         CUdeviceptr w = DP(W), xx = DP(X + (size_t)b0 * K), yy = DP(Y + (size_t)b0 * N);
         void *args[] = {&w, &xx, &yy, &K, &N};
-        int rc = sb_launch(c, f, gemv_grid(c, CEIL_DIV(N, 4), 8), 1, 256, (unsigned)(nb * K * 4), (CUstream)stream,
-                           args, 0);
+        int rc;
+        if (split_k) {
+            sb_fn_id f = nb == 4 ? F_GEMV_HH_SK4 : (nb == 2 ? F_GEMV_HH_SK2 : F_GEMV_HH_SK1);
+            rc = sb_launch(c, f, (unsigned)(tasks < 1 ? 1 : tasks), 1, 256, 0, (CUstream)stream, args, 0);
+        } else {
+            SB_ARG((size_t)nb * K * 4 <= 220 * 1024, "gemv_hh: batch x K too large for the shared x stage");
+            sb_fn_id f = nb == 4 ? F_GEMV_HH4 : (nb == 2 ? F_GEMV_HH2 : F_GEMV_HH1);
+            rc = sb_launch(c, f, gemv_grid(c, tasks, 8), 1, 256, (unsigned)(nb * K * 4), (CUstream)stream, args, 0);
+        }
         if (rc) return rc;
         b0 += nb;
     }

@@ -53,6 +53,9 @@ static const struct {
     [F_GEMV_HH1] = {M_QWEN, "gemv_hh1"},
     [F_GEMV_HH2] = {M_QWEN, "gemv_hh2"},
     [F_GEMV_HH4] = {M_QWEN, "gemv_hh4"},
+    [F_GEMV_HH_SK1] = {M_QWEN, "gemv_hh_sk1"},
+    [F_GEMV_HH_SK2] = {M_QWEN, "gemv_hh_sk2"},
+    [F_GEMV_HH_SK4] = {M_QWEN, "gemv_hh_sk4"},
     [F_RMSNORM] = {M_QWEN, "rmsnorm"},
     [F_ROPE] = {M_QWEN, "rope"},
     [F_SWIGLU] = {M_QWEN, "swiglu"},

@@ -95,10 +95,14 @@ def test_gemv_h_dropin_k_mod8_is_4(cuda_dev, qmod):
     _close(dy.cpu().numpy(), orc.gemv_h(W, x))
 
 
-@pytest.mark.parametrize("B", [1, 2, 3, 4, 8])
-@pytest.mark.parametrize("N,K", [(896, 896), (4864, 896), (896, 4864), (1003, 8192)])
+@pytest.mark.parametrize("B", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("N,K", [(896, 896), (4864, 896), (896, 4864), (1003, 8192), (3, 8), (7, 13696),
+                                 (1180, 1024), (1184, 1024)])
 def test_gemv_hh_batched(cuda_dev, B, N, K):
-    """FP16 activations (the GEMV sweep's x), batch B: y_b = W h2f(x_b)."""
+    """FP16 activations (the GEMV sweep's x), batch B: y_b = W h2f(x_b).
+    Fewer than 2 x SMs four-row tasks (N < 1184 on 148 SMs) take the split-K
+    kernels, the rest the warp-per-task ones; both sides of the switch, ragged
+    row tails and K slices shorter than a warp's stride are covered."""
     import torch
     W = _wh(N, K, 17)
     X = sb200.synth_normal_h(B * K, 1.0, 18).reshape(B, K)
