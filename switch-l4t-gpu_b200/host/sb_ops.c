@@ -208,6 +208,10 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     if (N == 0) return 0;
+    /* Up to 4 activation rows against a short weight matrix: the CUDA-core
+     * split-K GEMV beats a tcgen05 pass plus its split-K reduction
+     * (896 x 896, 4 rows: 3.6 against 6.9 us on B200). */
+    if (B <= 4 && CEIL_DIV(N, 4) < 2L * c->sms) return sb_gemv_hh(W, X, Y, K, N, B, stream);
     const int n_pad = CEIL_DIV(B, 16) * 16;
     CUtensorMap tw, tx;
     int rc = encode_kmajor_fp16(&tw, W, K, N, 128);
