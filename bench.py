@@ -478,7 +478,7 @@ def gemv_section(torch, dev):
                                      "launches": "CUDA-graph replay of %d" % reps}
     del pool
     torch.cuda.empty_cache()
-    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1, or gemv_hh_sk1 (split-K) below 2 x SMs four-row tasks (CUDA cores); b4, b16: sb_gemm_hh = gemm_hh_tc (tcgen05), except b4 on matrices of at most 16 MiB: gemv_hh4 / gemv_hh_sk4",
+    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1, or gemv_hh_sk1 (split-K) below 2 x SMs four-row tasks (CUDA cores); b4, b16: gemm_hh_tc (tcgen05)",
             "peak": peak, "unit": "GB/s", "shapes": out}
 
 

@@ -208,12 +208,6 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     if (N == 0) return 0;
-    /* Up to 4 activation rows against a weight matrix of at most 16 MiB:
-     * the CUDA-core GEMV is faster than a tcgen05 pass (4 rows on B200:
-     * 896 x 896 3.4 against 6.9 us, 4864 x 896 6.3 against 7.8 us, equal at
-     * 1003 x 8192); larger matrices are bandwidth-bound and the tensor
-     * cores keep up with HBM where the CUDA-core FMAs do not. */
-    if (B <= 4 && (size_t)N * K * 2 <= ((size_t)16 << 20)) return sb_gemv_hh(W, X, Y, K, N, B, stream);
     const int n_pad = CEIL_DIV(B, 16) * 16;
     CUtensorMap tw, tx;
     int rc = encode_kmajor_fp16(&tw, W, K, N, 128);
