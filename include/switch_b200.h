@@ -75,7 +75,9 @@ int sb_fma_peak(float *out, int iters, int grid, void *stream, double *flops);
 /* ---- GEMV ------------------------------------------------------------------
  * y[n] = sum_k W[n][k] x[k] (+ bias[n] if bias), W row-major [N][K].
  * FP32 weights: gemv / gemv4 / gemv_warp / gemv_warp_b (gemv.cu:3-71,
- * gpt2_kernels.cu:38-108).  K % 4 == 0. */
+ * gpt2_kernels.cu:38-108).  K % 4 == 0.  Outputs shorter than 8 rows per
+ * SM run split-K (K divided over a CTA's warps); longer ones stage x in
+ * shared memory and need K <= 51200. */
 int sb_gemv_f32(const float *W, const float *x, const float *bias, float *y, int K, int N, void *stream);
 /* Y[t][n] = sum_k W[n][k] X[t][k] (+ bias[n]) for T token rows
  * (gemv_multi, gpt2_kernels.cu:115-155). */
@@ -83,7 +85,8 @@ int sb_gemv_multi_f32(const float *W, const float *X, const float *bias, float *
                       void *stream);
 /* FP16 weights (raw IEEE half bits, exponent-0 values read as 0 as in the
  * reference's h2f), FP32 x, y, bias: gemv_h (qwen_kernels.cu:34-70).
- * K % 8 == 0. */
+ * K % 8 == 0.  Outputs shorter than 8 rows per SM run split-K; longer ones
+ * stage x in shared memory and need K <= 51200. */
 int sb_gemv_h(const uint16_t *W, const float *x, const float *bias, float *y, int K, int N, void *stream);
 /* FP16 weights and FP16 activations, batch B in 1..8: Y[b][n] =
  * sum_k h2f(W[n][k]) h2f(X[b][k]), FP32 accumulate and output (the GEMV

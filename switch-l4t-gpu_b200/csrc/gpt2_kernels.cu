@@ -218,6 +218,21 @@ extern "C" __global__ void __launch_bounds__(256) gemv_f32_b200(const float *__r
     }
 }
 
+// gemv_f32_b200 for short outputs: split-K over a CTA's warps
+// (splitk_rows4), x read through L1.  Block 256, no dynamic shared memory,
+// K % 4 == 0.
+extern "C" __global__ void __launch_bounds__(256) gemv_f32_sk(const float *__restrict__ W,
+                                                              const float *__restrict__ x,
+                                                              const float *__restrict__ bias,
+                                                              float *__restrict__ y, int K, int N) {
+    const uint4 *W4 = reinterpret_cast<const uint4 *>(W);
+    const int cpr = K / 4;
+    const XGlob4 xa{x};
+    splitk_rows4(N, cpr, bias, y, [&](const int (&rows)[4], int cb, int ce, float (&acc)[4]) {
+        warp_dot_f_range<4, 4>(W4, cpr, rows, cb, ce, xa, acc);
+    });
+}
+
 // MHA decode attention with an explicit T; one query head per KV slot.
 extern "C" __global__ void attn_decode_g1(const float *__restrict__ q, const float *__restrict__ kc,
                                           const float *__restrict__ vc, int T, float *__restrict__ out,

@@ -171,6 +171,20 @@ extern "C" __global__ void __launch_bounds__(256) gemv_h_b200(const unsigned sho
     }
 }
 
+// gemv_h_b200 for short outputs: split-K over a CTA's warps (splitk_rows4),
+// x read through L1.  Block 256, no dynamic shared memory, K % 8 == 0.
+extern "C" __global__ void __launch_bounds__(256) gemv_h_sk(const unsigned short *__restrict__ W,
+                                                            const float *__restrict__ x,
+                                                            const float *__restrict__ bias,
+                                                            float *__restrict__ y, int K, int N) {
+    const uint4 *W4 = reinterpret_cast<const uint4 *>(W);
+    const int cpr = K / 8;
+    const XGlob8 xa{x};
+    splitk_rows4(N, cpr, bias, y, [&](const int (&rows)[4], int cb, int ce, float (&acc)[4]) {
+        warp_dot_h_range<4, 4>(W4, cpr, rows, cb, ce, xa, acc);
+    });
+}
+
 // Y[b][n] = sum_k h2f(W[n][k]) h2f(X[b][k]) for B activation rows (fp16,
 // decoded with the same flush-to-zero rule), FP32 out, on sm_100's
 // mixed-precision FMA (each step equal to fmaf on the decoded values, in the

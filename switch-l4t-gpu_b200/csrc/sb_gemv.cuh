@@ -308,3 +308,37 @@ SB_DEV void warp_dot_hb(const uint4 *W, long ld_chunks, const int (&rows)[R], in
 #pragma unroll
         for (int b = 0; b < B; b++) acc[r][b] = warp_sum(acc[r][b]);
 }
+
+// Split-K task loop for short outputs (fewer four-row tasks than two per
+// SM, where a warp per task would leave most SMs idle): one CTA per task;
+// its 8 warps (block 256) take contiguous eighths of the row's `cpr` chunks,
+// `dot(rows, cb, ce, acc)` leaves each warp's reduced partials in acc, and
+// the partials are added in warp order in shared memory.  y[row] = sum
+// (+ bias[row]).
+template <class Dot>
+SB_DEV void splitk_rows4(int N, int cpr, const float *bias, float *y, Dot dot) {
+    constexpr int R = 4, NW = 8;
+    __shared__ float part[NW][R];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = (cpr + NW - 1) / NW;
+    const int cb = min(cpr, warp * per), ce = min(cpr, cb + per);
+    for (int t = blockIdx.x; t < (N + R - 1) / R; t += gridDim.x) {
+        int rows[R];
+        consecutive_rows<R>(t * R, N, rows);
+        float acc[R];
+        dot(rows, cb, ce, acc);
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < R; r++) part[warp][r] = acc[r];
+        }
+        __syncthreads();
+        if (threadIdx.x < R) {
+            const int row = t * R + threadIdx.x;
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) s += part[w][threadIdx.x];
+            if (row < N) y[row] = s + (bias ? bias[row] : 0.0f);
+        }
+        __syncthreads();  // part is reused by the CTA's next task
+    }
+}

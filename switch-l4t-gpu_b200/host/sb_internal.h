@@ -37,6 +37,8 @@ typedef enum {
     F_GEMV_HH_SK1,
     F_GEMV_HH_SK2,
     F_GEMV_HH_SK4,
+    F_GEMV_H_SK,
+    F_GEMV_F32_SK,
     F_RMSNORM,
     F_ROPE,
     F_SWIGLU,

@@ -66,11 +66,14 @@ static unsigned gemv_grid(sb_ctx *c, long tasks, int warps) {
 int sb_gemv_f32(const float *W, const float *x, const float *bias, float *y, int K, int N, void *stream) {
     SB_ARG(W && x && y && K > 0 && N >= 0, "bad GEMV arguments");
     SB_ARG(K % 4 == 0 && ALIGNED16(W) && ALIGNED16(x), "gemv_f32 needs K % 4 == 0 and 16-byte aligned W, x");
-    SB_ARG((size_t)K * 4 <= 200 * 1024, "gemv_f32: K too large for the shared x stage");
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     CUdeviceptr w = DP(W), xx = DP(x), b = DP(bias), yy = DP(y);
     void *args[] = {&w, &xx, &b, &yy, &K, &N};
+    const long tasks = CEIL_DIV(N, 4);
+    if (tasks < 2L * c->sms) /* short output: split-K over a CTA per four-row task */
+        return sb_launch(c, F_GEMV_F32_SK, (unsigned)(tasks < 1 ? 1 : tasks), 1, 256, 0, (CUstream)stream, args, 0);
+    SB_ARG((size_t)K * 4 <= 200 * 1024, "gemv_f32: K too large for the shared x stage");
     return sb_launch(c, F_GEMV_F32_B200, gemv_grid(c, CEIL_DIV(N, 4), 8), 1, 256, (unsigned)K * 4,
                      (CUstream)stream, args, 0);
 }
@@ -89,11 +92,14 @@ int sb_gemv_multi_f32(const float *W, const float *X, const float *bias, float *
 int sb_gemv_h(const uint16_t *W, const float *x, const float *bias, float *y, int K, int N, void *stream) {
     SB_ARG(W && x && y && K > 0 && N >= 0, "bad GEMV arguments");
     SB_ARG(K % 8 == 0 && ALIGNED16(W) && ALIGNED16(x), "gemv_h needs K % 8 == 0 and 16-byte aligned W, x");
-    SB_ARG((size_t)K * 4 <= 200 * 1024, "gemv_h: K too large for the shared x stage");
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     CUdeviceptr w = DP(W), xx = DP(x), b = DP(bias), yy = DP(y);
     void *args[] = {&w, &xx, &b, &yy, &K, &N};
+    const long tasks = CEIL_DIV(N, 4);
+    if (tasks < 2L * c->sms) /* short output: split-K over a CTA per four-row task */
+        return sb_launch(c, F_GEMV_H_SK, (unsigned)(tasks < 1 ? 1 : tasks), 1, 256, 0, (CUstream)stream, args, 0);
+    SB_ARG((size_t)K * 4 <= 200 * 1024, "gemv_h: K too large for the shared x stage");
     return sb_launch(c, F_GEMV_H_B200, gemv_grid(c, CEIL_DIV(N, 4), 8), 1, 256, (unsigned)K * 4,
                      (CUstream)stream, args, 0);
 }

@@ -56,6 +56,8 @@ static const struct {
     [F_GEMV_HH_SK1] = {M_QWEN, "gemv_hh_sk1"},
     [F_GEMV_HH_SK2] = {M_QWEN, "gemv_hh_sk2"},
     [F_GEMV_HH_SK4] = {M_QWEN, "gemv_hh_sk4"},
+    [F_GEMV_H_SK] = {M_QWEN, "gemv_h_sk"},
+    [F_GEMV_F32_SK] = {M_GPT2, "gemv_f32_sk"},
     [F_RMSNORM] = {M_QWEN, "rmsnorm"},
     [F_ROPE] = {M_QWEN, "rope"},
     [F_SWIGLU] = {M_QWEN, "swiglu"},
