@@ -110,6 +110,30 @@ def test_large_rows_and_freivalds(cuda_dev):
     assert orc.freivalds(A, B, C) > 1e-5
 
 
+def test_16384_sampled_rows_and_freivalds(cuda_dev):
+    """The largest SGEMM config (16384^3, 3 GB of operands and result): the
+    harness's triple loop on sampled rows, and an FP64 Freivalds check of
+    the whole product, where the full CPU loop would take hours."""
+    import torch
+    n = 16384
+    A, B = _mats(n, n, n, 16384)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dC = torch.zeros((n, n), device="cuda")
+    sb200.sgemm(dA, dB, dC, n, n, n)
+    torch.cuda.synchronize()
+    del dA, dB
+    C = dC.cpu().numpy()
+    del dC
+    for r in (0, 8191, 16383):
+        ref = orc.sgemm(A, B, r, r + 1)[r]
+        assert _rel_frob(C[r], ref) <= REL_FROB
+    assert orc.freivalds(A, B, C) < 1e-5
+    # one wrong cell is visible: |C| ~ 43 here and ||A.B.r|| ~ 7e5, so an
+    # error of 100 in one cell moves the check to ~1.4e-4
+    C[12345, 678] += 100.0
+    assert orc.freivalds(A, B, C) > 1e-5
+
+
 def test_row_panels_assemble(cuda_dev):
     """sb_sgemm_rows over 4 panels (the multi-GPU shard unit) equals one call."""
     import torch
