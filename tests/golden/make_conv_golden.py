@@ -10,7 +10,9 @@ blocks (so a mismatch can be located).
 
 Run from the repository root:
     python tests/golden/make_conv_golden.py [reference checkout]
-(default: $SB_REFERENCE_DIR, else /root/reference).  Needs ~4 GB of /tmp.
+(default: $SB_REFERENCE_DIR, else the build machine's reference checkout,
+the same default as __graft_entry__.build()).  Needs ~4 GB of temporary
+space.
 """
 import hashlib
 import json
