@@ -34,6 +34,16 @@ def test_matches_reference_converter(model, tmp_path):
         pytest.fail(f"{model}: output differs from the reference converter's in 64 MiB blocks {bad}")
 
 
+def test_gpt2_prefixed_names(tmp_path):
+    """Checkpoints saved from GPT2LMHeadModel name the tensors
+    'transformer.h.0...': same values, so the same output bytes."""
+    g = GOLD["gpt2"]
+    src, dst = str(tmp_path / "p.safetensors"), str(tmp_path / "p.bin")
+    conv_synth.write(src, [("transformer." + n, shp) for n, shp in conv_synth.gpt2_tensors()], "F32", g["seed"])
+    sb_convert.convert("gpt2", src, dst)
+    assert make_conv_golden.file_digest(dst)[1] == g["sha256"]
+
+
 def _tiny_safetensors(path, tensors):
     """tensors: {name: (dtype string, ndarray of the stored type)}"""
     header, off, blobs = {}, 0, []
