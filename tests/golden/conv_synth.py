@@ -69,8 +69,9 @@ def _values(seed, index, start, n):
 
 def write(path, tensors, dtype, seed, threads=8):
     """Write a safetensors file holding `tensors` [(name, shape)] in `dtype`
-    ('BF16' or 'F32').  BF16 keeps the top half of each FP32 value."""
-    esz = 2 if dtype == "BF16" else 4
+    ('BF16', 'F16' or 'F32').  BF16 keeps the top half of each FP32 value;
+    F16 rounds it to nearest even."""
+    esz = 4 if dtype == "F32" else 2
     order = sorted(range(len(tensors)), key=lambda i: _mix64(seed * 7919 + i))  # storage order
     header, off = {}, 0
     for i in order:
@@ -99,6 +100,8 @@ def write(path, tensors, dtype, seed, threads=8):
         v = _values(seed, i, s, n)
         if dtype == "BF16":
             data[a + 2 * s:a + 2 * (s + n)] = (v.view(np.uint32) >> np.uint32(16)).astype(np.uint16).view(np.uint8)
+        elif dtype == "F16":
+            data[a + 2 * s:a + 2 * (s + n)] = v.astype(np.float16).view(np.uint8)
         else:
             data[a + 4 * s:a + 4 * (s + n)] = v.view(np.uint8)
 

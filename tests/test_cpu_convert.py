@@ -44,6 +44,42 @@ def test_gpt2_prefixed_names(tmp_path):
     assert make_conv_golden.file_digest(dst)[1] == g["sha256"]
 
 
+def test_qwen_f16_source_is_copied_exactly(tmp_path):
+    """An F16 checkpoint (conv_qwen.py:38-39 widens it to FP32 and rounds
+    back): every weight lands in the file bit for bit, at the engine's
+    offsets (embedding, fused q|k|v rows and biases, gate|up rows, down
+    rows, final norm)."""
+    V, C, NL, QKV, FC, CTX, HD = 151936, 896, 24, 1152, 4864, 8192, 64
+    src, dst = str(tmp_path / "q16.safetensors"), str(tmp_path / "q16.bin")
+    conv_synth.write(src, conv_synth.qwen_tensors(), "F16", 20261231)
+    sb_convert.convert("qwen", src, dst)
+    st = sb_convert.SafeTensors(src)
+    out = np.memmap(dst, dtype=np.uint8, mode="r")
+
+    def raw(*names):
+        return np.concatenate([np.ascontiguousarray(st.raw(n)).view(np.uint8).ravel() for n in names])
+
+    lbase = V * C * 2 + 2 * CTX * (HD // 2) * 4
+    lstride = (C + QKV * C + QKV + C * C + C + 2 * FC * C + C * FC) * 2
+    assert np.array_equal(out[:V * C * 2], raw("model.embed_tokens.weight"))
+    for layer in (0, 13, NL - 1):
+        p, base = f"model.layers.{layer}.", lbase + layer * lstride
+        qkvw = base + C * 2
+        qkvb = qkvw + QKV * C * 2
+        post = qkvb + QKV * 2 + C * C * 2
+        gateup = post + C * 2
+        down = gateup + 2 * FC * C * 2
+        assert np.array_equal(out[base:qkvw], raw(p + "input_layernorm.weight"))
+        assert np.array_equal(out[qkvw:qkvb], raw(p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
+                                                  p + "self_attn.v_proj.weight"))
+        assert np.array_equal(out[qkvb:qkvb + QKV * 2], raw(p + "self_attn.q_proj.bias", p + "self_attn.k_proj.bias",
+                                                            p + "self_attn.v_proj.bias"))
+        assert np.array_equal(out[gateup:down], raw(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"))
+        assert np.array_equal(out[down:down + C * FC * 2], raw(p + "mlp.down_proj.weight"))
+    lnf = lbase + NL * lstride
+    assert np.array_equal(out[lnf:], raw("model.norm.weight"))
+
+
 def _tiny_safetensors(path, tensors):
     """tensors: {name: (dtype string, ndarray of the stored type)}"""
     header, off, blobs = {}, 0, []
