@@ -87,14 +87,41 @@ def weights_path():
     return os.path.join(d, f"qwen_{WEIGHT_SEED}.bin")
 
 
+QWEN_FILE_BYTES = 990162688  # the reference's Qwen weight-file size (qwen_engine.c:61-75)
+QWEN_V = 151936
+
+
+def synth_tool():
+    """The stand-alone synthetic-input writer (bin/sb_synth: sb_synth.c only,
+    no CUDA and no libswitch_b200.so), so the reference arm never maps this
+    package's GPU library."""
+    exe = os.path.join(PKG, "bin", "sb_synth")
+    if not os.access(exe, os.X_OK):
+        raise RuntimeError("switch-l4t-gpu_b200/bin/sb_synth is not built (run __graft_entry__.build())")
+    return exe
+
+
 def ensure_weights(barrier):
-    import sb200
     path = weights_path()
-    if LOCAL_RANK == 0 and not (os.path.exists(path) and os.path.getsize(path) == sb200.QWEN["FILE_BYTES"]):
+    if LOCAL_RANK == 0 and not (os.path.exists(path) and os.path.getsize(path) == QWEN_FILE_BYTES):
         tmp = path + f".tmp{os.getpid()}"
-        sb200.synth_weights(sb200.MODEL_QWEN, tmp, WEIGHT_SEED)
+        subprocess.run([synth_tool(), "weights", "qwen", tmp, str(WEIGHT_SEED)], check=True, stdout=subprocess.DEVNULL)
         os.replace(tmp, path)
     barrier()
+    return path
+
+
+def prompt_ids(seed, n=N_PROMPT, vocab=QWEN_V):
+    """The benchmark prompt (sb_synth_ids of `seed`), via bin/sb_synth."""
+    out = subprocess.run([synth_tool(), "ids", str(n), str(vocab), str(seed)], check=True, capture_output=True,
+                         text=True).stdout.split()
+    return [int(v) for v in out]
+
+
+def prompt_file(seed):
+    path = os.path.join(os.path.dirname(weights_path()), f"prompt_{seed}_{N_PROMPT}.txt")
+    with open(path, "w") as f:
+        f.write("\n".join(str(i) for i in prompt_ids(seed)) + "\n")
     return path
 
 
@@ -184,40 +211,53 @@ def ref_bench_exe():
     return exe if os.access(exe, os.X_OK) else None
 
 
-def run_ref_bench(path, procs, warmup, steps, tokens):
+def run_ref_bench(path, procs, warmup, steps, tokens, prompt=None):
     exe = ref_bench_exe()
-    out = subprocess.run([exe, path, str(procs), str(warmup), str(steps), str(tokens), "42"],
-                         capture_output=True, text=True, timeout=1800)
+    cmd = [exe, path, str(procs), str(warmup), str(steps), str(tokens), "42"] + ([prompt] if prompt else [])
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
     if out.returncode != 0:
         raise RuntimeError(f"ref_qwen_bench failed: {out.stderr[-400:]}")
     return json.loads(out.stdout.strip().splitlines()[-1])
 
 
+PROMPT_SEED = 1000  # rank r of the GPU arm uses PROMPT_SEED + r; the CPU legs use rank 0's prompt
+
+
 def cpu_baseline(path):
-    """Reference CPU decode on this host's cores, bounded sample (rank 0, N=1)."""
+    """Reference CPU decode on this host's cores, bounded sample (rank 0, N=1):
+    the same 32-token prompt primed untimed, then decode from position 32 on,
+    as the GPU arm does."""
     cores = host_cores()
     if ref_bench_exe():
-        r = run_ref_bench(path, cores, 0, 1, CPU_SAMPLE_TOKENS)
+        r = run_ref_bench(path, cores, 0, 1, CPU_SAMPLE_TOKENS, prompt_file(PROMPT_SEED))
         return {"value": round(r["tok_s"], 4), "unit": UNIT, "cores": cores, "kind": "reference",
-                "sample": f"{cores} forked replicas of the reference cpu_forward (qwen_engine.c:292-358) + argmax, "
-                          f"{CPU_SAMPLE_TOKENS} greedy decode tokens each; {r['timed_s']:.1f} s wall"}
+                "sample": f"{cores} forked replicas of the reference cpu_forward (qwen_engine.c:292-358) + argmax: "
+                          f"the {N_PROMPT}-token prompt primed untimed, then {CPU_SAMPLE_TOKENS} greedy decode "
+                          f"tokens each from position {N_PROMPT}; {r['timed_s']:.1f} s timed"}
     # oracle restatement (row-parallel threads) when the reference build is absent
     sys.path.insert(0, os.path.join(REPO, "tests"))
     import numpy as np
     import orc
-    m = orc.Model("qwen", path, 8, 151936)
-    m.forward(42, 0, True)
+    m = orc.Model("qwen", path, N_PROMPT + 8, QWEN_V)
+    ids = prompt_ids(PROMPT_SEED)
+    for p_, t in enumerate(ids):
+        logits = m.forward(t, p_, p_ == len(ids) - 1, nthreads=cores)
+    tok = int(np.argmax(logits))
     t0 = time.perf_counter()
-    tok = 42
-    for p in range(1, 3):
-        tok = int(np.argmax(m.forward(tok, p, True, nthreads=cores)))
+    for p_ in range(N_PROMPT, N_PROMPT + 2):
+        tok = int(np.argmax(m.forward(tok, p_, True, nthreads=cores)))
     dt = time.perf_counter() - t0
     m.close()
     return {"value": round(2 / dt, 4), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": "oracle restatement of cpu_forward, rows split over threads, 2 decode tokens"}
+            "sample": f"oracle restatement of cpu_forward, rows split over threads: prompt primed, "
+                      f"2 decode tokens from position {N_PROMPT}"}
 
 
 def run_reference_arm(args):
+    """The reference's own CPU decode (cpu_forward + argmax of qwen_engine.c,
+    compiled unmodified into oracle/_ref/ref_qwen_bench) on this host's
+    cores.  This process maps no library of this package: the weight file
+    and prompt come from bin/sb_synth, a separate CUDA-free program."""
     if RANK != 0:
         return
     line = {"impl": "reference", "metric": METRIC, "unit": UNIT, "higher_is_better": True}
@@ -225,17 +265,20 @@ def run_reference_arm(args):
         line["unavailable"] = "oracle/_ref/ref_qwen_bench not built (needs the reference sources at build time)"
         print(json.dumps(line))
         return
-    import sb200  # noqa: F401  (synthetic weight writer)
     path = ensure_weights(lambda: None)
     cores = host_cores()
-    r = run_ref_bench(path, cores, args.warmup, args.steps, 2)
+    r = run_ref_bench(path, cores, args.warmup, args.steps, 2, prompt_file(PROMPT_SEED))
     step_ms = 1e3 * r["timed_s"] / r["steps"]
     line.update({
         "value": round(r["tok_s"], 4), "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_ms, 3), "scaling": "weak", "vs_baseline": None, "dtype": "f16w-f32",
-        "data": "synthetic", "config": dict(CONFIG, impl="reference CPU (single-threaded engine, one replica per core)"),
+        "data": "synthetic",
+        "config": dict(CONFIG, global_batch=WORLD, seq_len=N_PROMPT + N_GEN,
+                       parallelism=f"replicas x{WORLD} (decode does not shard)"),
         "cpu_baseline": {"value": round(r["tok_s"], 4), "unit": UNIT, "cores": cores, "kind": "reference",
-                         "sample": f"per step: {cores} replicas x 2 greedy decode tokens of the reference cpu_forward"},
+                         "sample": f"per step: {cores} forked replicas x 2 greedy decode tokens of the reference "
+                                   f"cpu_forward, positions {N_PROMPT}+ after the same {N_PROMPT}-token prompt "
+                                   f"(primed untimed) as the GPU arm"},
         "e2e": {"value": round(r["tok_s"], 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
     print(json.dumps(line))
@@ -260,9 +303,53 @@ def fp32_peak_tflops(torch, dev):
     return flops / (e0.elapsed_time(e1) * 1e-3) / 1e12
 
 
+def gathered_c_check(torch, dev, ps, B, n, dist_on):
+    """Verify the all-gathered C on this rank without any CPU oracle: FP64
+    Freivalds (C r against A (B r) for the WHOLE matrix, every rank's panel
+    of A regenerated from its seed) and exact FP64 rows (4 per panel)
+    against the harness rule |c - ref| <= 0.05 |ref| + 1e-3
+    (gpu_workload.c:99-101).  Returns (freivalds rel err, sampled-row rel
+    err, cells outside the rule), each the max over ranks."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    r = torch.rand(n, generator=g, device=dev, dtype=torch.float64) * 2 - 1
+    Bd = B.double()
+    Br = Bd @ r
+    lhs = ps.C.double() @ r
+    rhs = torch.empty(n, dtype=torch.float64, device=dev)
+    rows, idx = [], []
+    for q in range(ps.world):
+        r0, r1 = sgemm_dist_bounds(n, q, ps.world)
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(5000 + q)
+        Aq = torch.rand(r1 - r0, n, generator=gq, device=dev) * 2 - 1
+        rhs[r0:r1] = Aq.double() @ Br
+        pick = [0, (r1 - r0) // 3, 2 * (r1 - r0) // 3, r1 - r0 - 1]
+        rows.append(Aq[pick].double())
+        idx += [r0 + k for k in pick]
+        del Aq
+    fr = float(torch.linalg.norm(lhs - rhs) / torch.linalg.norm(rhs))
+    want = torch.cat(rows) @ Bd
+    got = ps.C[idx].double()
+    rel = float(torch.linalg.norm(got - want) / torch.linalg.norm(want))
+    bad = float(((got - want).abs() > 0.05 * want.abs() + 1e-3).sum())
+    t = torch.tensor([fr, rel, bad], dtype=torch.float64, device=dev)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    del Bd, Br, lhs, rhs, want, got
+    return float(t[0]), float(t[1]), int(t[2])
+
+
+def sgemm_dist_bounds(M, rank, world):
+    import sgemm_dist
+    return sgemm_dist.panel_bounds(M, rank, world)
+
+
 def sgemm_section(torch, dev, dist_on, steps, warmup, kernel="fp32"):
     """16384^3 FP32 SGEMM row-panel sharded over all ranks (strong scaling):
-    compute-only and with the NCCL all-gather of C, max over ranks.
+    compute-only and with the NCCL all-gather of C, max over ranks; at N > 1
+    also the chunked form (4 row chunks, each gathered while the next is
+    multiplied) and a check of the gathered C on every rank.
     kernel "3xtf32" is the opt-in tensor-pipe variant (reported separately)."""
     import sgemm_dist
     n = SGEMM_N
@@ -301,23 +388,43 @@ def sgemm_section(torch, dev, dist_on, steps, warmup, kernel="fp32"):
     torch.cuda.synchronize()
     comp = sum(a.elapsed_time(b) for a, b, _ in evs)
     tot = sum(a.elapsed_time(c) for a, _, c in evs)
-    t = torch.tensor([comp, tot], dtype=torch.float64, device=dev)
+    ov = 0.0
+    if ps.world > 1:  # chunked: the gather of chunk i overlaps the product of chunk i + 1
+        pc = sgemm_dist.PanelSgemm(n, n, n, kernel=kernel, chunks=4)
+        for _ in range(max(1, warmup)):
+            pc(A, B)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for _ in range(steps):
+            pc(A, B)
+        e1.record(cur)
+        torch.cuda.synchronize()
+        ov = e0.elapsed_time(e1)
+        del pc
+        torch.cuda.empty_cache()
+    t = torch.tensor([comp, tot, ov], dtype=torch.float64, device=dev)
     if dist_on:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    comp_ms, tot_ms = float(t[0]) / steps, float(t[1]) / steps
+    comp_ms, tot_ms, ov_ms = float(t[0]) / steps, float(t[1]) / steps, float(t[2]) / steps
+    # the result every rank holds after the gather, checked on every rank
+    ps(A, B)
+    torch.cuda.synchronize()
+    fr, rel, bad = gathered_c_check(torch, dev, ps, B, n, dist_on)
+    verdict = "CORRECT" if fr <= 1e-5 and rel <= 1e-5 and bad == 0 else "WRONG"
     flop = 2.0 * n ** 3
     per_gpu = 2.0 * ps.rows * n * n / (comp_ms * 1e-3) / 1e12
-    res = {"metric": "SGEMM TFLOPS", "n": n, "value": round(flop / (tot_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-           "compute_tflops": round(flop / (comp_ms * 1e-3) / 1e12, 2), "ms_per_step": round(tot_ms, 3),
-           "compute_ms": round(comp_ms, 3), "allgather_ms": round(tot_ms - comp_ms, 3), "n_gpus": WORLD,
-           "scaling": "strong", "steps": steps,
-           "parallelism": f"row panels x{WORLD}, B replicated" + (", NCCL all-gather of C" if WORLD > 1 else ""),
-           "kernel": ("sgemm_b200 (FP32 FFMA2, 128x128x8 tiles, 2 CTAs/SM)" if kernel == "fp32" else
-                      "sgemm_3xtf32_tc (tcgen05 kind::tf32, 3xTF32 split, 128x128x32 tiles, B transposed once)"),
-           "dtype": "f32",
-           "roofline": {"bound": bound, "achieved": round(per_gpu, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
-                        "frac": round(per_gpu / peak, 4), "peak_source": peak_src},
-           "l2": "no flush: 1 GiB operands > 126 MB L2"}
+    res = {"n": n, "n_gpus": WORLD, "kernel": "sgemm_b200" if kernel == "fp32" else "sgemm_3xtf32_tc",
+           "value": round(flop / (tot_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "compute_tflops": round(flop / (comp_ms * 1e-3) / 1e12, 2), "compute_ms": round(comp_ms, 3),
+           "allgather_ms": round(tot_ms - comp_ms, 3), "ms_per_step": round(tot_ms, 3)}
+    if ov_ms:
+        res["chunked4_ms"] = round(ov_ms, 3)
+        res["chunked4_tflops"] = round(flop / (ov_ms * 1e-3) / 1e12, 2)
+    res.update({"check": {"verdict": verdict, "freivalds": float("%.2e" % fr), "rows_rel": float("%.2e" % rel),
+                          "bad_cells": bad},
+                "roofline": {"bound": bound, "achieved_per_gpu": round(per_gpu, 2), "peak": round(peak, 2),
+                             "frac": round(per_gpu / peak, 4), "peak_src": peak_src}})
     del A, B, ps
     torch.cuda.empty_cache()
     return res
@@ -580,7 +687,7 @@ def run_b200(args):
 
     eng = sb200.Engine(sb200.MODEL_QWEN, path, MAX_CTX)
     ext = torch.cuda.ExternalStream(eng.stream, device=dev)
-    prompt = sb200.synth_ids(N_PROMPT, sb200.QWEN["V"], 1000 + RANK)
+    prompt = sb200.synth_ids(N_PROMPT, sb200.QWEN["V"], PROMPT_SEED + RANK)
 
     def decode_step():
         """One request with resident inputs: returns decode-loop ms (events)."""
@@ -696,8 +803,9 @@ def run_b200(args):
     }
     eng.close()
     if not args.no_secondary:
-        line["sgemm"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3)
-        line["sgemm_3xtf32"] = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3, kernel="3xtf32")
+        # measured here, printed last (see below)
+        sg = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3)
+        sg3 = sgemm_section(torch, dev, dist, max(3, args.steps // 2), 3, kernel="3xtf32")
         line["gemv"] = gemv_section(torch, dev)
         line["gpt2_decode"] = gpt2_section(torch, dev, dist, max(3, args.steps // 2), 3, not args.no_cpu_baseline)
     if RANK == 0 and WORLD == 1 and not args.no_cpu_baseline:
@@ -712,8 +820,16 @@ def run_b200(args):
                 line["gemv"]["cpu_baseline"] = extra["gemv_cpu"]
             except Exception as ex:  # reported, not fatal
                 line["sgemm_1024"] = {"error": str(ex)[:200]}
+    if not args.no_secondary:
+        # the strong-scaling SGEMM rows of configs[4] close the line, so a
+        # reader that keeps only its tail still has them at every N
+        line["sgemm_note"] = ("configs[4]: 16384^3 FP32 row panels over n_gpus ranks, B replicated, NCCL "
+                              "all-gather of C; value includes the gather; per-GPU roofline vs the live FMA peak; "
+                              "gathered C checked on every rank (FP64 Freivalds + exact rows)")
+        line["sgemm"] = sg
+        line["sgemm_3xtf32"] = sg3
     if RANK == 0:
-        print(json.dumps(line))
+        print(json.dumps(line, separators=(",", ":")))
     if dist:
         import torch.distributed as tdist
         barrier()

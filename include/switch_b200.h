@@ -133,9 +133,11 @@ int sb_attn_decode(const float *q, const float *kc, const float *vc, float *out,
  * (a fixed device budget sized at start-up, a host framework that owns every
  * allocation, an allocation-free token loop): the partials and tickets live
  * in a static array compiled into this library, at most T <= 2048 positions
- * and NH <= 16 heads (larger requests return SB_ERR_ARG).  The first call on
- * a device resolves that array's address (make it before any stream capture
- * begins); all calls share the array, so calls that overlap on the GPU race.
+ * and NH <= 16 heads (larger requests return SB_ERR_ARG).  The array exists
+ * once per CUDA context (a device's primary context or one the host created);
+ * the first call in a context resolves its address there (make it before any
+ * stream capture begins); all calls in a context share the array, so calls
+ * that overlap on the GPU race.
  * No counterpart in the reference, which has no scratch-using kernel. */
 int sb_attn_decode_noalloc(const float *q, const float *kc, const float *vc, float *out, int T, int NH, int NKV,
                            int HD, int kv_stride, float scale, void *stream);
@@ -193,6 +195,13 @@ int sb_engine_finish(sb_engine *e, int *out_ids, int *n_out);
 void *sb_engine_stream(sb_engine *e);
 /* Device pointer of the logits buffer (V floats) and the vocabulary size. */
 int sb_engine_logits(sb_engine *e, const float **dev_logits, int *vocab);
+/* The engine's KV cache (the reference's kc / vc device buffers,
+ * qwen_engine.c:83,180-181 and gpt2_engine.c:82,149-150, sized by max_ctx instead of
+ * the file's CTX): FP32 [2][layers][max_ctx][width] -- keys for every layer,
+ * then values -- with width 128 (Qwen, 2 KV heads x 64) or 768 (GPT-2).  A
+ * host may read it, or write positions the next steps will attend to (a
+ * cached prefix), between steps on sb_engine_stream(). */
+int sb_engine_kv_cache(sb_engine *e, void **dev_kv, size_t *bytes, int *layers, int *max_ctx, int *width);
 /* Kernel launches issued per decode step (with / without LM head). */
 int sb_engine_launches_per_step(sb_engine *e, int with_logits);
 /* 1 when the step runs as the persistent whole-step kernel (GPUs with >= 128

@@ -318,6 +318,7 @@ void orc_qwen_reset(orc_qwen *m) {
     memset(m->vc, 0, sizeof(float) * (size_t)QNL * m->ctx * QKVD);
 }
 const float *orc_qwen_residual(const orc_qwen *m) { return m->x; }
+float *orc_qwen_kv(orc_qwen *m, int which) { return which ? m->vc : m->kc; }
 void orc_qwen_close(orc_qwen *m) {
     if (!m) return;
     munmap((void *)m->file, m->size);
@@ -407,6 +408,7 @@ void orc_gpt2_reset(orc_gpt2 *m) {
     memset(m->vc, 0, sizeof(float) * (size_t)GNL * m->ctx * GC);
 }
 const float *orc_gpt2_residual(const orc_gpt2 *m) { return m->x; }
+float *orc_gpt2_kv(orc_gpt2 *m, int which) { return which ? m->vc : m->kc; }
 void orc_gpt2_close(orc_gpt2 *m) {
     if (!m) return;
     munmap((void *)m->w, m->size);

@@ -91,6 +91,10 @@ void orc_qwen_forward(orc_qwen *m, int token, int pos, int want_logits, float *l
                       int nthreads);
 /* Residual stream after the last forward's layers (C floats). */
 const float *orc_qwen_residual(const orc_qwen *m);
+/* The model's KV cache, which 0: keys, 1: values, each [NL][ctx][KVD] FP32
+ * (the reference's kc_h / vc_h), writable so a test can plant a long
+ * cached context without priming it token by token. */
+float *orc_qwen_kv(orc_qwen *m, int which);
 void orc_qwen_close(orc_qwen *m);
 
 typedef struct orc_gpt2 orc_gpt2;
@@ -100,6 +104,8 @@ void orc_gpt2_reset(orc_gpt2 *m);
 void orc_gpt2_forward(orc_gpt2 *m, int token, int pos, int want_logits, float *logits,
                       int nthreads);
 const float *orc_gpt2_residual(const orc_gpt2 *m);
+/* which 0: keys, 1: values, each [NL][ctx][C] FP32. */
+float *orc_gpt2_kv(orc_gpt2 *m, int which);
 void orc_gpt2_close(orc_gpt2 *m);
 
 /* First index of the maximum (strict >), qwen_engine.c:360-364. */

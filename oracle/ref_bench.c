@@ -4,12 +4,19 @@
  * `--impl reference` legs.  Test/measurement infrastructure only.
  *
  *   ref_<model>_bench <weights> <procs> <warmup> <steps> <tokens_per_step> <first_token>
+ *                     [prompt_ids_file]
  *
  * The weight file is loaded once; then <procs> forked replicas (sharing the
  * weights copy-on-write) each run a greedy decode -- cpu_forward with logits,
  * then the reference argmax -- for (warmup + steps) x tokens_per_step
- * positions.  The reference engine is single-threaded, so replicas are how
- * it uses several cores.  Prints one JSON line: per-step wall time (max over
+ * positions.  With a prompt file (ids, one per line) every replica first
+ * primes that prompt as the reference's generation loop does
+ * (qwen_engine.c:523-541: cpu_forward per prompt position, logits at the
+ * last, argmax -> first generated token), untimed, and the timed decode
+ * continues from position n_prompt; without one it decodes from position 0
+ * starting at <first_token>.  All replicas start the timed steps together.
+ * The reference engine is single-threaded, so replicas are how it uses
+ * several cores.  Prints one JSON line: per-step wall time (max over
  * replicas) and aggregate decode tokens/s over the timed steps. */
 #define _GNU_SOURCE
 #include <stdio.h>
@@ -42,12 +49,26 @@ static double now_s(void) {
 
 int main(int argc, char **argv) {
     if (argc < 7) {
-        fprintf(stderr, "usage: %s weights procs warmup steps tokens_per_step first_token\n", argv[0]);
+        fprintf(stderr, "usage: %s weights procs warmup steps tokens_per_step first_token [prompt_ids]\n", argv[0]);
         return 2;
     }
     const int procs = atoi(argv[2]), warmup = atoi(argv[3]), steps = atoi(argv[4]);
     const int tps = atoi(argv[5]), first = atoi(argv[6]);
     if (procs < 1 || steps < 1 || tps < 1) return 2;
+    int *prompt = NULL, n_prompt = 0;
+    if (argc > 7) {
+        FILE *pf = fopen(argv[7], "r");
+        if (!pf) return 2;
+        int cap = 64, v;
+        prompt = malloc(sizeof(int) * cap);
+        while (fscanf(pf, "%d", &v) == 1) {
+            if (v < 0 || v >= VOCAB) return 2;
+            if (n_prompt == cap) prompt = realloc(prompt, sizeof(int) * (cap *= 2));
+            prompt[n_prompt++] = v;
+        }
+        fclose(pf);
+        if (n_prompt < 1) return 2;
+    }
     /* the reference loader prints a banner on stdout: keep stdout for JSON */
     int saved = dup(1);
     dup2(2, 1);
@@ -56,8 +77,8 @@ int main(int argc, char **argv) {
     dup2(saved, 1);
     close(saved);
 
-    int go[2], res[2];
-    if (pipe(go) || pipe(res)) return 3;
+    int go[2], res[2], ready[2], go2[2];
+    if (pipe(go) || pipe(res) || pipe(ready) || pipe(go2)) return 3;
     const int nsteps = warmup + steps;
     for (int p = 0; p < procs; p++) {
         pid_t pid = fork();
@@ -69,6 +90,12 @@ int main(int argc, char **argv) {
             if (read(go[0], &c, 1) != 1) _exit(4);
             float *logits = malloc(sizeof(float) * VOCAB);
             int tok = (first + 7919 * p) % VOCAB, pos = 0;
+            if (n_prompt > 0) {
+                for (pos = 0; pos < n_prompt; pos++) FORWARD(prompt[pos], pos, pos == n_prompt - 1, logits);
+                tok = ref_argmax_any(logits, VOCAB);
+            }
+            /* every replica starts its timed steps together, after all have primed */
+            if (write(ready[1], &c, 1) != 1 || read(go2[0], &c, 1) != 1) _exit(4);
             double *dt = malloc(sizeof(double) * nsteps);
             for (int s = 0; s < nsteps; s++) {
                 double t0 = now_s();
@@ -84,10 +111,18 @@ int main(int argc, char **argv) {
     }
     close(go[0]);
     close(res[1]);
+    close(ready[1]);
+    close(go2[0]);
     char ones[4096];
     memset(ones, 1, sizeof ones);
     for (int p = 0; p < procs; p += 4096)
         if (write(go[1], ones, (size_t)(procs - p < 4096 ? procs - p : 4096)) < 0) return 3;
+    for (int p = 0; p < procs; p++) {
+        char c;
+        if (read(ready[0], &c, 1) != 1) break; /* a replica died: its result is missing below */
+    }
+    for (int p = 0; p < procs; p += 4096)
+        if (write(go2[1], ones, (size_t)(procs - p < 4096 ? procs - p : 4096)) < 0) return 3;
     double *mx = calloc(nsteps, sizeof(double));
     double *buf = malloc(sizeof(double) * nsteps);
     int got = 0;
@@ -108,8 +143,8 @@ int main(int argc, char **argv) {
     double timed = 0;
     for (int s = warmup; s < nsteps; s++) timed += mx[s];
     printf("{\"procs\":%d,\"replicas_ok\":%d,\"warmup\":%d,\"steps\":%d,\"tokens_per_step\":%d,"
-           "\"timed_s\":%.6f,\"tok_s\":%.6f,\"step_s\":[",
-           procs, got, warmup, steps, tps, timed, got * (double)tps * steps / timed);
+           "\"n_prompt\":%d,\"first_pos\":%d,\"timed_s\":%.6f,\"tok_s\":%.6f,\"step_s\":[",
+           procs, got, warmup, steps, tps, n_prompt, n_prompt, timed, got * (double)tps * steps / timed);
     for (int s = warmup; s < nsteps; s++) printf("%s%.6f", s > warmup ? "," : "", mx[s]);
     printf("]}\n");
     return got == procs ? 0 : 1;

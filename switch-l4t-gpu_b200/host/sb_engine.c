@@ -414,6 +414,16 @@ int sb_engine_logits(sb_engine *e, const float **dev_logits, int *vocab) {
     return 0;
 }
 
+int sb_engine_kv_cache(sb_engine *e, void **dev_kv, size_t *bytes, int *layers, int *max_ctx, int *width) {
+    if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);
+    if (dev_kv) *dev_kv = (void *)(uintptr_t)e->kv;
+    if (bytes) *bytes = (size_t)2 * e->NL * e->ctx_cap * e->kvw * 4;
+    if (layers) *layers = e->NL;
+    if (max_ctx) *max_ctx = e->ctx_cap;
+    if (width) *width = e->kvw;
+    return 0;
+}
+
 int sb_engine_launches_per_step(sb_engine *e, int with_logits) {
     if (!e) return 0;
     if (e->mk) return 1;

@@ -74,6 +74,7 @@ typedef enum {
 
 typedef struct sb_ctx {
     CUcontext ctx;
+    unsigned long long ctx_id; /* cuCtxGetId: unique for the process's life */
     CUdevice dev;
     CUmodule mod[M_COUNT];
     CUfunction fn[F_COUNT];

@@ -18,9 +18,10 @@
 // and stays resident on every GPU that loads the library until the process
 // exits.
 //
-// Set-up: the first call on a device looks up the array's device address
-// with cudaGetSymbolAddress while that device is current (one lookup per
-// device, cached); make that first call before any stream capture begins.
+// Set-up: the first call in a CUDA context (a device's primary context, or a
+// context the host created itself) looks up the array's device address with
+// cudaGetSymbolAddress while that context is current (one lookup per
+// context, cached); make that first call before any stream capture begins.
 // Every call shares the one array and it keeps the previous call's
 // contents: each call clears the tickets it uses (they must start at zero)
 // on its stream before launching.  Calls that can overlap on the GPU (two
@@ -50,25 +51,40 @@ __global__ void attn_decode_noalloc_kernel(const float *__restrict__ q, const fl
     attn_decode_body<G>(q, kc, vc, T, out, scratch, tickets, kv_stride, scale, max_splits);
 }
 
-#define SB_NOALLOC_MAX_DEVICES 64
-static float *scratch_addr[SB_NOALLOC_MAX_DEVICES];
+// The array exists once per CUDA context that loads this library's module
+// (the primary context of a device, or any context a host created with
+// cuCtxCreate, as the reference's hosts do), so its address is looked up --
+// and cached -- per context.  Contexts are told apart by cuCtxGetId, which
+// is unique for the life of the process, so a context created after another
+// was destroyed never inherits the old context's address.
+#define SB_NOALLOC_MAX_CONTEXTS 64
+static unsigned long long scratch_ctx_id[SB_NOALLOC_MAX_CONTEXTS];
+static float *scratch_addr[SB_NOALLOC_MAX_CONTEXTS];
+static int scratch_n;
 static pthread_mutex_t scratch_lock = PTHREAD_MUTEX_INITIALIZER;
 
 static int device_scratch(float **out) {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return sb_fail(SB_ERR_STATE, cudaGetErrorString(e), __FILE__, __LINE__);
-    if (dev < 0 || dev >= SB_NOALLOC_MAX_DEVICES)
-        return sb_fail(SB_ERR_STATE, "device ordinal beyond the no-alloc table", __FILE__, __LINE__);
+    // the library's context rule: the calling thread's current context, else
+    // device 0's primary context made current
+    const sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    const unsigned long long id = c->ctx_id;
+    float *p = nullptr;
     pthread_mutex_lock(&scratch_lock);
-    if (!scratch_addr[dev]) {
-        void *p = nullptr;
-        e = cudaGetSymbolAddress(&p, sb_noalloc_scratch);
-        if (e == cudaSuccess) scratch_addr[dev] = static_cast<float *>(p);
+    for (int i = 0; i < scratch_n; i++)
+        if (scratch_ctx_id[i] == id) p = scratch_addr[i];
+    if (!p && scratch_n < SB_NOALLOC_MAX_CONTEXTS) {
+        void *a = nullptr;
+        if (cudaGetSymbolAddress(&a, sb_noalloc_scratch) == cudaSuccess && a) {
+            p = static_cast<float *>(a);
+            scratch_ctx_id[scratch_n] = id;
+            scratch_addr[scratch_n++] = p;
+        }
     }
-    float *p = scratch_addr[dev];
     pthread_mutex_unlock(&scratch_lock);
-    if (!p) return sb_fail(SB_ERR_STATE, "cudaGetSymbolAddress(sb_noalloc_scratch) failed", __FILE__, __LINE__);
+    if (!p)
+        return sb_fail(SB_ERR_STATE, "cudaGetSymbolAddress(sb_noalloc_scratch) failed (or more than 64 contexts)",
+                       __FILE__, __LINE__);
     *out = p;
     return 0;
 }

@@ -136,14 +136,22 @@ sb_ctx *sb_ctx_get(void) {
         sb_fail(SB_ERR_STATE, "no current CUDA context", __FILE__, __LINE__);
         return NULL;
     }
+    /* keyed by the context's id, not its handle: a context created after
+     * another was destroyed may reuse the old handle value */
+    unsigned long long id = 0;
+    if (cuCtxGetId(cur, &id) != CUDA_SUCCESS) {
+        sb_fail(SB_ERR_STATE, "cuCtxGetId", __FILE__, __LINE__);
+        return NULL;
+    }
     pthread_mutex_lock(&ctx_lock);
     sb_ctx *found = NULL;
     for (int i = 0; i < nctx; i++)
-        if (ctxs[i].ctx == cur) found = &ctxs[i];
+        if (ctxs[i].ctx_id == id) found = &ctxs[i];
     if (!found && nctx < SB_MAX_CTX) {
         sb_ctx *c = &ctxs[nctx];
         memset(c, 0, sizeof *c);
         c->ctx = cur;
+        c->ctx_id = id;
         if (load_modules(c) == 0) { found = c; nctx++; }
     } else if (!found) {
         sb_fail(SB_ERR_STATE, "too many CUDA contexts", __FILE__, __LINE__);

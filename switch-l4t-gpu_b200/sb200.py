@@ -95,6 +95,7 @@ def lib():
     _sig(L.sb_engine_create, P, I, ctypes.c_char_p, I, ctypes.c_uint)
     _sig(L.sb_engine_destroy, None, P)
     _sig(L.sb_engine_reset, I, P)
+    _sig(L.sb_engine_kv_cache, I, P, P, P, P, P, P)
     _sig(L.sb_engine_forward, I, P, I, I, I, P)
     _sig(L.sb_engine_generate, I, P, P, I, I, P, ctypes.POINTER(I), ctypes.c_uint)
     _sig(L.sb_engine_begin, I, P, P, I, I, ctypes.c_uint)
@@ -345,6 +346,15 @@ class Engine:
     @property
     def persistent(self):
         return bool(lib().sb_engine_uses_persistent_kernel(self.h))
+
+    def kv_cache(self):
+        """(device pointer, bytes, layers, max_ctx, width) of the FP32
+        [2][layers][max_ctx][width] KV cache."""
+        p, nb = ctypes.c_void_p(), ctypes.c_size_t()
+        nl, ctx, w = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        check(lib().sb_engine_kv_cache(self.h, ctypes.byref(p), ctypes.byref(nb), ctypes.byref(nl), ctypes.byref(ctx),
+                                       ctypes.byref(w)))
+        return p.value, nb.value, nl.value, ctx.value, w.value
 
     def launches_per_step(self, with_logits=True):
         return lib().sb_engine_launches_per_step(self.h, 1 if with_logits else 0)

@@ -19,6 +19,27 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
 
 
+# Parity margins: the engine tests record their worst per-step error next to
+# the bar it must stay under; the session summary prints them, so a drift
+# toward a bar is visible in a passing run.
+MARGINS = {}
+
+
+def record_margin(name, err, bar):
+    prev = MARGINS.get(name)
+    if prev is None or err > prev[0]:
+        MARGINS[name] = (float(err), float(bar))
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    if not MARGINS:
+        return
+    terminalreporter.section("parity margins (worst error / bar)")
+    for name in sorted(MARGINS):
+        err, bar = MARGINS[name]
+        terminalreporter.write_line(f"{name}: {err:.3e} / {bar:.0e}  ({100 * err / bar:.1f}% of the bar)")
+
+
 def _weights_dir():
     d = os.environ.get("SB_WEIGHTS_DIR") or ("/dev/shm/sb200_weights" if os.path.isdir("/dev/shm") else "/tmp/sb200_weights")
     os.makedirs(d, exist_ok=True)

@@ -44,7 +44,9 @@ def file_digest(path):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SB_REFERENCE_DIR", "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SB_REFERENCE_DIR", "")
+    if not ref:
+        sys.exit("usage: make_conv_golden.py <reference checkout>  (or set SB_REFERENCE_DIR)")
     tools = os.path.join(ref, "gpu-llm", "tools")
     out = {"block_bytes": BLOCK}
     with tempfile.TemporaryDirectory() as tmp:

@@ -52,6 +52,8 @@ def oracle():
         getattr(L, f"orc_{n}_residual").argtypes = [P]
         getattr(L, f"orc_{n}_residual").restype = P
         getattr(L, f"orc_{n}_close").argtypes = [P]
+        getattr(L, f"orc_{n}_kv").argtypes = [P, I]
+        getattr(L, f"orc_{n}_kv").restype = P
     L.orc_argmax.argtypes = [P, I]
     L.orc_argmax.restype = I
     _orc = L
@@ -176,6 +178,17 @@ class Model:
 
     def reset(self):
         getattr(oracle(), f"orc_{self.name}_reset")(self.h)
+
+    def kv(self, ctx, layers, width):
+        """The KV cache as one writable (2, layers, ctx, width) FP32 view:
+        [0] keys, [1] values (the oracle keeps them as two arrays, so this
+        returns a pair of (layers, ctx, width) views)."""
+        out = []
+        for which in (0, 1):
+            ptr = getattr(oracle(), f"orc_{self.name}_kv")(self.h, which)
+            buf = (ctypes.c_float * (layers * ctx * width)).from_address(ptr)
+            out.append(np.ctypeslib.as_array(buf).reshape(layers, ctx, width))
+        return out
 
     def close(self):
         if self.h:

@@ -1,0 +1,93 @@
+"""The reference-compatible command-line hosts on the GPU: the Qwen engine's
+`--serve` wire protocol (gpu-llm/engine/qwen_engine.c:406-444, read by
+gpu-llm/server/qwen_serve.py), `--ids`/`--gen` greedy generation into
+out.ids for both engines (qwen_engine.c:523-556, gpt2_engine.c:540-573),
+and gemv_test's verdict lines (gpu-llm/harness/gemv_test.c).  Each output
+is checked against the oracle's restatement of the reference's greedy loop
+on the same weight file."""
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import orc
+import sb200
+
+pytestmark = pytest.mark.gpu
+BIN = os.path.join(os.path.dirname(sb200.__file__), "bin")
+QW_EOS = (151643, 151645)
+G2_EOS = (50256,)
+
+
+def _write_ids(path, ids):
+    with open(path, "wb") as f:
+        f.write(struct.pack("<I", len(ids)))
+        f.write(struct.pack(f"<{len(ids)}I", *ids))
+
+
+def _read_ids(path):
+    with open(path, "rb") as f:
+        n = struct.unpack("<I", f.read(4))[0]
+        return list(struct.unpack(f"<{n}I", f.read(4 * n)))
+
+
+def _oracle_greedy(name, weights, vocab, prompt, n_gen, eos):
+    ref = orc.Model(name, weights, len(prompt) + n_gen + 8, vocab)
+    try:
+        ids, _ = orc.greedy(ref, prompt, n_gen, eos)
+    finally:
+        ref.close()
+    return ids
+
+
+def test_qwen_serve_two_requests(cuda_dev, qwen_weights):
+    """Two framed requests on one process (u32 T, T x u32 ids, u32 max_gen ->
+    u32 M, M x u32 ids: prompt echo + generation), greedy; each reply equals
+    the oracle's greedy loop, and the second request is not disturbed by the
+    first one's cache."""
+    V = sb200.QWEN["V"]
+    reqs = [(sb200.synth_ids(11, V, 501), 7), (sb200.synth_ids(5, V, 502), 12)]
+    stdin = b"".join(struct.pack("<I", len(p)) + struct.pack(f"<{len(p)}I", *p) + struct.pack("<I", g)
+                     for p, g in reqs)
+    out = subprocess.run([os.path.join(BIN, "qwen_engine"), "--weights", str(qwen_weights), "--serve", "--greedy",
+                          "--ctx", "256"], input=stdin, capture_output=True, timeout=300)
+    assert out.returncode == 0, out.stderr.decode()[-800:]
+    buf = out.stdout
+    for prompt, maxg in reqs:
+        m = struct.unpack("<I", buf[:4])[0]
+        got = list(struct.unpack(f"<{m}I", buf[4:4 + 4 * m]))
+        buf = buf[4 + 4 * m:]
+        want = _oracle_greedy("qwen", qwen_weights, V, prompt, maxg, QW_EOS)
+        assert got == want
+    assert buf == b""  # nothing else on stdout: banners go to stderr
+    assert out.stderr.decode().count("serve: T=") == 2
+
+
+@pytest.mark.parametrize("model", ["qwen", "gpt2"])
+def test_engine_cli_greedy_out_ids(cuda_dev, qwen_weights, gpt2_weights, tmp_path, model):
+    """`--ids F --gen N` writes prompt + generated ids to out.ids in the
+    working directory, prints the reference's summary lines and ENGINE_DONE."""
+    if model == "qwen":
+        exe, w, V, eos, extra = "qwen_engine", qwen_weights, sb200.QWEN["V"], QW_EOS, ["--greedy", "--ctx", "128"]
+    else:
+        exe, w, V, eos, extra = "gpt2_engine", gpt2_weights, sb200.GPT2["V"], G2_EOS, ["--ctx", "128"]
+    prompt = sb200.synth_ids(9, V, 777)
+    _write_ids(tmp_path / "p.ids", prompt)
+    out = subprocess.run([os.path.join(BIN, exe), "--weights", str(w), "--ids", "p.ids", "--gen", "10"] + extra,
+                         capture_output=True, text=True, timeout=300, cwd=tmp_path)
+    assert out.returncode == 0, out.stderr[-800:]
+    assert "prompt: 9 token(s)" in out.stdout and out.stdout.rstrip().endswith("ENGINE_DONE")
+    assert _read_ids(tmp_path / "out.ids") == _oracle_greedy(model, w, V, prompt, 10, eos)
+
+
+def test_gemv_test_cli(cuda_dev):
+    """gemv_test <module> N K: every kernel of the M0 module CORRECT against
+    the harness's CPU loop, then GEMV_TEST_DONE."""
+    out = subprocess.run([os.path.join(BIN, "gemv_test"), sb200.CUBINS["gemv"], "1000", "772"], capture_output=True,
+                         text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-800:]
+    for name in ("gemv", "gemv4", "gemv_warp"):
+        assert f"{name}: CORRECT" in out.stdout
+    assert out.stdout.rstrip().endswith("GEMV_TEST_DONE")

@@ -9,6 +9,7 @@ import pytest
 
 import orc
 import sb200
+from conftest import record_margin
 
 pytestmark = pytest.mark.gpu
 LOGIT_TOL = 2e-3
@@ -28,6 +29,7 @@ def _teacher_forced(model_id, weights, vocab, ctx, ids, flags=0):
             eng.forward(t, p, True, got)
             want = ref.forward(t, p, True)
             assert np.isfinite(got).all()
+            record_margin(f"{name} teacher-forced logits (flags {flags})", _rel(got, want), LOGIT_TOL)
             assert _rel(got, want) <= LOGIT_TOL, f"pos {p}: rel err {_rel(got, want):.2e}"
             assert int(np.argmax(got)) == int(np.argmax(want))
     finally:
@@ -192,10 +194,58 @@ def test_long_context_decode(cuda_dev, qwen_weights, gpt2_weights, model):
             for k in range(n_dec):
                 got = np.zeros(V, dtype=np.float32)
                 eng.forward(toks[k], n_prompt - 1 + k, True, got)
+                record_margin(f"{model} 600-token context logits (flags {flags})", _rel(got, wants[k]), LOGIT_TOL)
                 assert _rel(got, wants[k]) <= LOGIT_TOL, f"flags {flags} step {k}: {_rel(got, wants[k]):.2e}"
                 assert int(np.argmax(got)) == toks[k + 1]
         finally:
             eng.close()
+
+
+@pytest.mark.parametrize("model,ctx,start,n_dec,flags", [
+    ("qwen", 2048, 2036, 4, 0), ("qwen", 2048, 2036, 2, sb200.FLAG_MULTI_KERNEL),
+    ("gpt2", 1024, 1020, 4, 0), ("gpt2", 1024, 1020, 2, sb200.FLAG_MULTI_KERNEL),
+    ("qwen", 8192, 8188, 2, 0)])
+def test_decode_at_kv_cap(cuda_dev, qwen_weights, gpt2_weights, model, ctx, start, n_dec, flags):
+    """Decode steps at the end of a full KV cache: configs[2]'s cap of 2048
+    positions (GPT-2: its file's 1024; Qwen also at the reference's CTX of
+    8192, where the persistent kernel must still be chosen).  Positions
+    [0, start) hold the same planted cache in the engine (through
+    sb_engine_kv_cache) and in the oracle, so no 2000-token priming is
+    needed; then n_dec teacher-forced steps attend over up to ctx positions
+    and their logits are compared with the oracle's.  At these lengths the
+    persistent kernel's attention items hold 255-1024 positions each, far
+    past the 64 kept in registers: the shared-memory score path runs."""
+    import ctypes
+
+    import drv
+    mid, w, V = ((sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"]) if model == "qwen"
+                 else (sb200.MODEL_GPT2, gpt2_weights, sb200.GPT2["V"]))
+    eng = sb200.Engine(mid, w, ctx, flags)
+    ref = orc.Model(model, w, ctx, V)
+    try:
+        if flags == 0:
+            assert eng.persistent == (sb200.sm_count() >= 128)
+        ptr, nbytes, NL, cap, width = eng.kv_cache()
+        assert cap == ctx and nbytes == 2 * NL * ctx * width * 4
+        rng = np.random.default_rng(start + ctx)
+        kv = np.zeros((2, NL, ctx, width), dtype=np.float32)
+        kv[:, :, :start] = rng.uniform(-1.0, 1.0, (2, NL, start, width)).astype(np.float32)
+        drv.check(drv.cuda().cuMemcpyHtoD_v2(ctypes.c_uint64(ptr), kv.ctypes.data_as(ctypes.c_void_p),
+                                             ctypes.c_size_t(kv.nbytes)), "KV upload")
+        kc, vc = ref.kv(ctx, NL, width)
+        kc[:] = kv[0]
+        vc[:] = kv[1]
+        ids = sb200.synth_ids(n_dec, V, start)
+        for k in range(n_dec):
+            got = np.zeros(V, dtype=np.float32)
+            eng.forward(ids[k], start + k, True, got)
+            want = ref.forward(ids[k], start + k, True)
+            record_margin(f"{model} logits at the KV cap {ctx} (flags {flags})", _rel(got, want), LOGIT_TOL)
+            assert _rel(got, want) <= LOGIT_TOL, f"pos {start + k}: rel err {_rel(got, want):.2e}"
+            assert int(np.argmax(got)) == int(np.argmax(want))
+    finally:
+        eng.close()
+        ref.close()
 
 
 def test_engine_rejects_bad_input(cuda_dev, gpt2_weights, tmp_path):

@@ -157,3 +157,23 @@ def test_qwen_elementwise_dropins(cuda_dev, qmod):
     torch.cuda.synchronize()
     np.testing.assert_allclose(y.cpu().numpy(), orc.rmsnorm(x, w, 1e-6), rtol=2e-6, atol=1e-7)
     assert np.array_equal(a.cpu().numpy(), x + x)
+
+
+def test_gpt2_elementwise_dropins(cuda_dev, gmod):
+    """GPT-2's add_bias and add2 (gpt2_kernels.cu:209-217, both required by
+    gpt2_engine.c:124-125) under the stock launches: add2 as the residual
+    adds of gpt2_engine.c:220,249 (grid 3 x 256 over C = 768), add_bias over
+    the fc width, and a ragged n that leaves the last block partly idle."""
+    import torch
+    for n, grid in ((768, 3), (3072, 12), (1000, 4)):
+        a = sb200.synth_uniform(n, -2, 2, 20 + n)
+        b = sb200.synth_uniform(n, -2, 2, 21 + n)
+        out = torch.full((n + 64,), 7.0, device="cuda")  # the tail past n must stay untouched
+        gmod.launch("add2", (grid,), (256,), _t(a), _t(b), out, n)
+        y = torch.from_numpy(np.concatenate([a, np.full(64, 5.0, np.float32)])).cuda()
+        gmod.launch("add_bias", (grid,), (256,), y, _t(b), n)
+        torch.cuda.synchronize()
+        o = out.cpu().numpy()
+        assert np.array_equal(o[:n], a + b) and np.all(o[n:] == 7.0)
+        yy = y.cpu().numpy()
+        assert np.array_equal(yy[:n], a + b) and np.all(yy[n:] == 5.0)
