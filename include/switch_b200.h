@@ -65,6 +65,33 @@ int sb_sgemm(const float *A, const float *B, float *C, int M, int N, int K, void
 int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
                   void *stream);
 
+/* ---- multi-GPU SGEMM (row panels + NCCL all-gather of C), one rank per GPU.
+ * No counterpart in the reference, which runs on device 0 only
+ * (gpu_workload.c:66-67).  NCCL is loaded at run time (libnccl.so.2).
+ * Communicators are non-blocking: every wait polls ncclCommGetAsyncError
+ * against `timeout_s` and aborts the communicator (ncclCommAbort) when a
+ * peer never arrives or a collective never finishes, returning an error
+ * instead of hanging.  Call them with the rank's device context current. */
+/* A new NCCL unique id (ncclUniqueId, 128 bytes) for rank 0 to share. */
+int sb_nccl_unique_id(void *id128);
+/* ncclCommInitRankConfig (non-blocking) on the current context's device;
+ * *comm receives the ncclComm_t. */
+int sb_nccl_comm_init(void **comm, int world, const void *id128, int rank, double timeout_s);
+/* Finalise and destroy (aborts on failure or timeout). */
+int sb_nccl_comm_destroy(void *comm, double timeout_s);
+int sb_nccl_abort(void *comm);
+/* Rank `rank` of `world`: rows [rank R, min(M, rank R + R)) of C = A B
+ * (R = ceil(M / world)) with sb_sgemm_rows, then -- when gather != 0 -- an
+ * in-place ncclAllGather on `stream` so every rank holds all of C.  A and C
+ * point at full-size matrices on this rank's device (only this rank's rows
+ * of A are read); C must have room for world * R rows (the padding rows
+ * past M are scratch).  Asynchronous: follow with sb_nccl_wait. */
+int sb_sgemm_panel_allgather(const float *A, const float *B, float *C, int M, int N, int K, int rank, int world,
+                             void *comm, int gather, void *stream);
+/* Wait until `stream` is idle, watching `comm` (may be NULL) for errors;
+ * on an error or after timeout_s the communicator is aborted. */
+int sb_nccl_wait(void *comm, void *stream, double timeout_s);
+
 /* ---- bandwidth probe (membw_read4, gpu_workload.c:197-220) ---------------
  * out[i] (i < min(n4, grid*block)) = sum of this thread's float4s, `iters`
  * passes over buf[n4]; grid = 0 picks 4 CTAs per SM. */

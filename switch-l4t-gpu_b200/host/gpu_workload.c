@@ -2,7 +2,8 @@
  * reference harness's CLI and JSON contract (gpu_workload.c of
  * pkia/switch-l4t-gpu; consumed by deploy/cluster/gpu_task_example.py).
  *
- *   gpu_workload [--json] [--sizes 256,512,1024] [--membw-mib 2048] [--tf32x3] [module]
+ *   gpu_workload [--json] [--sizes 256,512,1024] [--membw-mib 2048] [--tf32x3]
+ *                [--gpus N [--dist-n 16384]] [module]
  *
  * `module` is a cubin/PTX image loaded with cuModuleLoadData (default: the
  * switch_gpu.cubin installed next to this binary).  Kernels are resolved by
@@ -20,9 +21,19 @@
  * JSON keys are the reference's (ptx, kernels, sgemm, sgemm4, sgemm_opt,
  * membw_gbps, done) plus additive ones (device, sm_count, sgemm_b200,
  * membw_bytes, fp32_peak_gflops_at_max_clock, and with --tf32x3 the opt-in
- * tensor-core SGEMM of this package: kernels.sgemm_3xtf32, sgemm_3xtf32). */
+ * tensor-core SGEMM of this package: kernels.sgemm_3xtf32, sgemm_3xtf32).
+ *
+ * --gpus N (additive; the reference has no multi-GPU path): after the suite,
+ * the dist-n^3 SGEMM sharded by row panels over devices 0..N-1, one host
+ * thread per device on its primary context, each rank computing its panel
+ * with sb_sgemm_rows and an in-place NCCL all-gather of C
+ * (sb_sgemm_panel_allgather over a non-blocking communicator with bounded
+ * waits).  Every rank then checks sampled cells of ALL panels of its
+ * gathered C against the harness's CPU loop and tolerance.  JSON key
+ * sgemm_dist; text line "sgemm_dist ...: CORRECT|WRONG". */
 #define _GNU_SOURCE
 #include <cuda.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -89,6 +100,103 @@ static int verify(const float *A, const float *B, const float *C, int n, int ful
     return bad;
 }
 
+/* ---- --gpus N: row-panel SGEMM + NCCL all-gather, one thread per device */
+typedef struct {
+    int rank, world, n;
+    const unsigned char *uid;
+    const float *hB; /* the replicated B, n x n, on the host */
+    double comp_ms, tot_ms;
+    int bad, checked, rc;
+    char msg[256];
+} dist_rank;
+
+#define DIST_SEED_A 5000ull
+#define DIST_CELLS 16 /* sampled cells per panel */
+#define DIST_TIMEOUT_S 120.0
+
+static void *dist_thread(void *p) {
+    dist_rank *a = p;
+    const int n = a->n, R = (n + a->world - 1) / a->world;
+    const int row0 = a->rank * R < n ? a->rank * R : n, row1 = row0 + R < n ? row0 + R : n;
+    CUdevice dev;
+    CUcontext ctx;
+    void *comm = NULL;
+    CUstream st = NULL;
+    CUdeviceptr dA = 0, dB = 0, dC = 0;
+    CUevent ev[4] = {NULL, NULL, NULL, NULL};
+    float *row = malloc((size_t)n * 4), *crow = malloc((size_t)n * 4);
+#define DFAIL(what) do { snprintf(a->msg, sizeof a->msg, "rank %d: %s: %s", a->rank, what, sb_last_error()); a->rc = 1; goto out; } while (0)
+#define DCK(x) do { if ((x) != CUDA_SUCCESS) DFAIL(#x); } while (0)
+    DCK(cuDeviceGet(&dev, a->rank));
+    DCK(cuDevicePrimaryCtxRetain(&ctx, dev));
+    DCK(cuCtxSetCurrent(ctx));
+    if (sb_nccl_comm_init(&comm, a->world, a->uid, a->rank, DIST_TIMEOUT_S)) DFAIL("communicator");
+    DCK(cuStreamCreate(&st, CU_STREAM_NON_BLOCKING));
+    const size_t nn = (size_t)n * n * 4;
+    DCK(cuMemAlloc(&dA, nn));
+    DCK(cuMemAlloc(&dB, nn));
+    DCK(cuMemAlloc(&dC, (size_t)a->world * R * n * 4));
+    for (int i = row0; i < row1; i++) { /* this rank's rows of A: row i from its own seeded stream */
+        sb_synth_uniform(row, (size_t)n, -1.0f, 1.0f, DIST_SEED_A + (uint64_t)i);
+        DCK(cuMemcpyHtoD(dA + (size_t)i * n * 4, row, (size_t)n * 4));
+    }
+    DCK(cuMemcpyHtoD(dB, a->hB, nn));
+    for (int k = 0; k < 4; k++) DCK(cuEventCreate(&ev[k], 0));
+    const float *pA = (const float *)(uintptr_t)dA, *pB = (const float *)(uintptr_t)dB;
+    float *pC = (float *)(uintptr_t)dC;
+    const int reps = 5;
+    for (int it = 0; it < 2 + reps; it++) { /* 2 warm-up iterations */
+        if (it == 2) DCK(cuEventRecord(ev[0], st));
+        if (sb_sgemm_panel_allgather(pA, pB, pC, n, n, n, a->rank, a->world, comm, 0, st)) DFAIL("panel");
+    }
+    DCK(cuEventRecord(ev[1], st));
+    DCK(cuEventRecord(ev[2], st));
+    for (int it = 0; it < reps; it++)
+        if (sb_sgemm_panel_allgather(pA, pB, pC, n, n, n, a->rank, a->world, comm, 1, st)) DFAIL("panel + gather");
+    DCK(cuEventRecord(ev[3], st));
+    if (sb_nccl_wait(comm, st, DIST_TIMEOUT_S)) DFAIL("wait");
+    float ms = 0;
+    DCK(cuEventElapsedTime(&ms, ev[0], ev[1]));
+    a->comp_ms = ms / reps;
+    DCK(cuEventElapsedTime(&ms, ev[2], ev[3]));
+    a->tot_ms = ms / reps;
+    /* the gathered C: sampled cells of every panel against the harness loop */
+    for (int q = 0; q < a->world; q++) {
+        const int q0 = q * R, q1 = q0 + R < n ? q0 + R : n;
+        for (int c = 0; c < DIST_CELLS && q1 > q0; c++) {
+            const int i = q0 + (int)(((long)c * 7919 + q * 131) % (q1 - q0));
+            const int j = (int)(((long)c * 104729 + q * 31 + 17) % n);
+            sb_synth_uniform(row, (size_t)n, -1.0f, 1.0f, DIST_SEED_A + (uint64_t)i);
+            float ref = 0; /* gpu_workload.c:97-98 */
+            for (int k = 0; k < n; k++) ref += row[k] * a->hB[(size_t)k * n + j];
+            DCK(cuMemcpyDtoH(crow, dC + ((size_t)i * n + j) * 4, 4));
+            float d = crow[0] - ref;
+            if (d < 0) d = -d;
+            if (d > 0.05f * (ref < 0 ? -ref : ref) + 1e-3f) a->bad++;
+            a->checked++;
+        }
+    }
+out:
+    for (int k = 0; k < 4; k++)
+        if (ev[k]) cuEventDestroy(ev[k]);
+    if (comm) {
+        if (a->rc) sb_nccl_abort(comm);
+        else if (sb_nccl_comm_destroy(comm, DIST_TIMEOUT_S)) {
+            snprintf(a->msg, sizeof a->msg, "rank %d: destroy: %s", a->rank, sb_last_error());
+            a->rc = 1;
+        }
+    }
+    if (dA) cuMemFree(dA);
+    if (dB) cuMemFree(dB);
+    if (dC) cuMemFree(dC);
+    if (st) cuStreamDestroy(st);
+    free(row);
+    free(crow);
+    return NULL;
+#undef DCK
+#undef DFAIL
+}
+
 typedef struct {
     const char *name, *json_key;
     CUfunction f;
@@ -101,7 +209,7 @@ int main(int argc, char **argv) {
     const char *mod_path = NULL;
     int sizes[16] = {256, 512, 1024}, nsizes = 3;
     long membw_mib = 2048;
-    int tf32x3 = 0;
+    int tf32x3 = 0, gpus = 0, dist_n = 16384;
     const char *v_t3 = NULL;
     double t3_ms[16] = {0}, t3_gf[16] = {0};
     for (int i = 1; i < argc; i++) {
@@ -111,6 +219,8 @@ int main(int argc, char **argv) {
             for (char *t = strtok(argv[++i], ","); t && nsizes < 16; t = strtok(NULL, ",")) sizes[nsizes++] = atoi(t);
         } else if (!strcmp(argv[i], "--membw-mib") && i + 1 < argc) membw_mib = atol(argv[++i]);
         else if (!strcmp(argv[i], "--tf32x3")) tf32x3 = 1;
+        else if (!strcmp(argv[i], "--gpus") && i + 1 < argc) gpus = atoi(argv[++i]);
+        else if (!strcmp(argv[i], "--dist-n") && i + 1 < argc) dist_n = atoi(argv[++i]);
         else mod_path = argv[i];
     }
     if (!mod_path) mod_path = default_module();
@@ -258,6 +368,50 @@ int main(int argc, char **argv) {
         cuMemFree(dout);
     }
 
+    /* ---- --gpus N: row-panel SGEMM over N devices + NCCL all-gather of C */
+    dist_rank dr[64];
+    double dist_comp = 0, dist_tot = 0;
+    int dist_bad = 0, dist_checked = 0;
+    if (gpus > 0) {
+        int ndev = 0;
+        CHK(cuDeviceGetCount(&ndev));
+        if (gpus > ndev || gpus > 64 || dist_n < 1) {
+            fprintf(stderr, "--gpus %d: only %d device(s) visible (or bad --dist-n)\n", gpus, ndev);
+            return 1;
+        }
+        unsigned char uid[128];
+        if (sb_nccl_unique_id(uid)) { fprintf(stderr, "%s\n", sb_last_error()); return 1; }
+        float *hB = malloc((size_t)dist_n * dist_n * 4);
+        for (int k = 0; k < dist_n; k++) /* row k of B from its own seeded stream */
+            sb_synth_uniform(hB + (size_t)k * dist_n, (size_t)dist_n, -1.0f, 1.0f, 777000ull + (uint64_t)k);
+        pthread_t th[64];
+        for (int r = 0; r < gpus; r++) {
+            memset(&dr[r], 0, sizeof dr[r]);
+            dr[r].rank = r;
+            dr[r].world = gpus;
+            dr[r].n = dist_n;
+            dr[r].uid = uid;
+            dr[r].hB = hB;
+            pthread_create(&th[r], NULL, dist_thread, &dr[r]);
+        }
+        int failed = 0;
+        for (int r = 0; r < gpus; r++) {
+            pthread_join(th[r], NULL);
+            if (dr[r].rc) { fprintf(stderr, "%s\n", dr[r].msg); failed = 1; }
+            if (dr[r].comp_ms > dist_comp) dist_comp = dr[r].comp_ms;
+            if (dr[r].tot_ms > dist_tot) dist_tot = dr[r].tot_ms;
+            dist_bad += dr[r].bad;
+            dist_checked += dr[r].checked;
+        }
+        free(hB);
+        CHK(cuCtxSetCurrent(ctx));
+        if (failed) return 1;
+        const double fl = 2.0 * dist_n * (double)dist_n * dist_n;
+        OUT("sgemm_dist %d^3 over %d GPU(s): compute %.3f ms (%.1f TFLOP/s), with all-gather %.3f ms (%.1f TFLOP/s); "
+            "%d cells of the gathered C checked on every rank: %s\n", dist_n, gpus, dist_comp, fl / (dist_comp * 1e9),
+            dist_tot, fl / (dist_tot * 1e9), dist_checked, dist_bad ? "WRONG" : "CORRECT");
+    }
+
     if (json_mode) {
         printf("{\"ptx\":\"");
         for (const char *p = mod_path; *p; p++) {
@@ -283,6 +437,13 @@ int main(int argc, char **argv) {
             for (int i = 0; i < nsizes; i++)
                 printf("%s{\"n\":%d,\"ms\":%.3f,\"gflops\":%.1f}", i ? "," : "", sizes[i], t3_ms[i], t3_gf[i]);
             printf("]");
+        }
+        if (gpus > 0) {
+            const double fl = 2.0 * dist_n * (double)dist_n * dist_n;
+            printf(",\"sgemm_dist\":{\"n\":%d,\"gpus\":%d,\"compute_ms\":%.3f,\"ms\":%.3f,\"allgather_ms\":%.3f,"
+                   "\"compute_tflops\":%.2f,\"tflops\":%.2f,\"cells_checked\":%d,\"verdict\":\"%s\"}",
+                   dist_n, gpus, dist_comp, dist_tot, dist_tot - dist_comp, fl / (dist_comp * 1e9),
+                   fl / (dist_tot * 1e9), dist_checked, dist_bad ? "WRONG" : "CORRECT");
         }
         printf(",\"membw_gbps\":%.1f,\"membw_bytes\":%.0f,\"device\":\"%s\",\"sm_count\":%d,"
                "\"fp32_peak_gflops_at_max_clock\":%.1f,\"done\":true}\n",

@@ -4,31 +4,37 @@
  *   qwen_engine --weights W.bin [--ptx M] [--ids F] [--gen N] [--selftest N]
  *               [--debug] [--greedy] [--serve] [--ctx N]
  *
- * The weight file is the reference's flat layout.  --ptx is accepted for
- * command-line compatibility; the sm_100a module images are linked into
- * libswitch_b200.  Generation follows the reference: prime the prompt
- * (logits on the last token only), then pick tokens greedily (--greedy) or
- * by the reference's sampler (temperature 0.7, top-k 20, top-p 0.8,
- * repetition penalty 1.1, xorshift seed 1234), stopping at <|endoftext|> or
- * <|im_end|>; out.ids receives prompt + generated ids; ENGINE_DONE last.
+ * The weight file is the reference's flat layout.  Generation follows the
+ * reference: prime the prompt (logits on the last token only), then pick
+ * tokens greedily (--greedy) or by the reference's sampler (temperature 0.7,
+ * top-k 20, top-p 0.8, repetition penalty 1.1, xorshift seed 1234),
+ * stopping at <|endoftext|> or <|im_end|>; out.ids receives prompt +
+ * generated ids; ENGINE_DONE last.
  *
- * Greedy generation runs entirely on the device (graph-replayed steps with
- * the argmax and next-token write fused); sampled generation copies the
- * logits back each token and samples on the host, as the reference does.
+ * Without --ptx every step is this package's fused engine: greedy generation
+ * runs entirely on the device (graph-replayed persistent step with the
+ * argmax and next-token write fused); sampled generation copies the logits
+ * back each token and samples on the host, as the reference does.
+ * --ptx M loads module image M and decodes through ITS drop-in kernels
+ * (gemv_h, rmsnorm, rope, swiglu, attn_*, add2) with the reference's
+ * per-stage launches (cli_refpath.c), as the reference host does.
  *
+ * --selftest N: decode ids[0..N-1] on the GPU (the engine, or module M) and
+ * with the serial CPU forward written in this host (cli_refpath.c), and
+ * compare the logits at position N-1: top-5 of each, max |gpu - cpu|,
+ * argmax MATCH -> "SELFTEST: PASS" (qwen_engine.c:494-521).
+ * --debug: the reference's layer-0 stage dumps at position 0 ("g.*" from a
+ * per-stage GPU pass, "c.*" from the CPU forward during --selftest).
  * --serve: per request read u32 T, T x u32 ids, u32 max_gen from stdin and
  * write u32 M, M x u32 ids (prompt echo + generation) to stdout; banners go
- * to stderr only (qwen_engine.c:406-444).
- * --selftest N: decode ids[0..N-1] through the graph-replayed fused step and
- * through direct launches without programmatic dependent launch, and compare
- * the last logits (top-5, max |diff|, argmax); the independent CPU golden
- * comparison is the parity test suite's job. */
+ * to stderr only (qwen_engine.c:406-444). */
 #define _GNU_SOURCE
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
+#include "cli_refpath.h"
 #include "sb_cli.h"
 
 #define V 151936
@@ -38,6 +44,13 @@
 static int greedy_mode = 0;
 static uint32_t rng_state = 1234;
 static float *scratch_logits, *sample_scratch;
+static refpath *modpath; /* --ptx: decode through the given module's kernels */
+
+/* one decode step with the reference's gpu_forward contract */
+static void gpu_forward(sb_engine *e, int token, int pos, int want_logits, float *logits) {
+    if (modpath) rp_forward(modpath, token, pos, want_logits, logits, 0);
+    else if (sb_engine_forward(e, token, pos, want_logits, logits)) cli_die("forward");
+}
 
 static int next_token(sb_engine *e, const int *ids, int n) {
     (void)e;
@@ -47,14 +60,13 @@ static int next_token(sb_engine *e, const int *ids, int n) {
 
 /* Sampled generation: forward per token with host logits. Returns total. */
 static int generate_sampled(sb_engine *e, int *ids, int total, int n_gen, int cap, int *emitted) {
-    for (int p = 0; p < total; p++)
-        if (sb_engine_forward(e, ids[p], p, p == total - 1, p == total - 1 ? scratch_logits : NULL)) cli_die("forward");
+    for (int p = 0; p < total; p++) gpu_forward(e, ids[p], p, p == total - 1, p == total - 1 ? scratch_logits : NULL);
     int nxt = next_token(e, ids, total);
     ids[total++] = nxt;
     *emitted = 0;
     for (int g = 0; g < n_gen && total < cap; g++) {
         if (nxt == EOT || nxt == IM_END) break;
-        if (sb_engine_forward(e, nxt, total - 1, 1, scratch_logits)) cli_die("forward");
+        gpu_forward(e, nxt, total - 1, 1, scratch_logits);
         nxt = next_token(e, ids, total);
         ids[total++] = nxt;
         (*emitted)++;
@@ -63,7 +75,7 @@ static int generate_sampled(sb_engine *e, int *ids, int total, int n_gen, int ca
 }
 
 static int generate(sb_engine *e, int *ids, int total, int n_gen, int cap, int *emitted) {
-    if (!greedy_mode) return generate_sampled(e, ids, total, n_gen, cap, emitted);
+    if (!greedy_mode || modpath) return generate_sampled(e, ids, total, n_gen, cap, emitted);
     if (total + n_gen > cap) n_gen = cap - total;
     int n = 0;
     if (sb_engine_generate(e, ids, total, n_gen, ids, &n, SB_GEN_STOP_EOS)) cli_die("generate");
@@ -109,11 +121,11 @@ static void serve_loop(sb_engine *e, int ctx) {
 
 int main(int argc, char **argv) {
     setvbuf(stdout, NULL, _IONBF, 0);
-    const char *weights = NULL, *ids_file = NULL;
+    const char *weights = NULL, *ids_file = NULL, *ptx = NULL;
     int n_gen = 24, selftest = 0, serve = 0, ctx = 2048, debug = 0;
     for (int i = 1; i < argc; i++) {
         if (!strcmp(argv[i], "--weights") && i + 1 < argc) weights = argv[++i];
-        else if (!strcmp(argv[i], "--ptx") && i + 1 < argc) ++i; /* images are built in */
+        else if (!strcmp(argv[i], "--ptx") && i + 1 < argc) ptx = argv[++i];
         else if (!strcmp(argv[i], "--ids") && i + 1 < argc) ids_file = argv[++i];
         else if (!strcmp(argv[i], "--gen") && i + 1 < argc) n_gen = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--selftest") && i + 1 < argc) selftest = atoi(argv[++i]);
@@ -126,19 +138,26 @@ int main(int argc, char **argv) {
     if (!weights) { fprintf(stderr, "--weights required\n"); return 2; }
     if (ctx < 32 || ctx > 8192) { fprintf(stderr, "--ctx must be in [32, 8192]\n"); return 2; }
     if (n_gen > ctx) n_gen = ctx;
-    (void)debug;
     FILE *log = serve ? stderr : stdout;
     double t0 = cli_now();
-    sb_engine *e = sb_engine_create(SB_MODEL_QWEN, weights, ctx, 0);
-    if (!e) cli_die("engine");
-    fprintf(log, "weights: %.1f MiB (24-layer Qwen2.5-0.5B, fp16); gpu ready in %.1f s (ctx %d)\n",
-            990162688 / 1048576.0, cli_now() - t0, ctx);
+    sb_engine *e = NULL;
+    if (ptx) {
+        modpath = rp_open(SB_MODEL_QWEN, weights, ptx, ctx);
+        fprintf(log, "weights: %.1f MiB (24-layer Qwen2.5-0.5B, fp16); module %s, per-stage launches (ctx %d)\n",
+                990162688 / 1048576.0, rp_module_name(modpath), ctx);
+    } else {
+        e = sb_engine_create(SB_MODEL_QWEN, weights, ctx, 0);
+        if (!e) cli_die("engine");
+        fprintf(log, "weights: %.1f MiB (24-layer Qwen2.5-0.5B, fp16); gpu ready in %.1f s (ctx %d)\n",
+                990162688 / 1048576.0, cli_now() - t0, ctx);
+    }
     scratch_logits = malloc(sizeof(float) * V);
     sample_scratch = malloc(sizeof(float) * V);
     if (serve) {
         fprintf(stderr, "serve mode: reading requests from stdin\n");
         serve_loop(e, ctx);
-        sb_engine_destroy(e);
+        if (e) sb_engine_destroy(e);
+        rp_close(modpath);
         return 0;
     }
     int *ids = malloc(sizeof(int) * (size_t)(2 * ctx + 2));
@@ -153,37 +172,48 @@ int main(int argc, char **argv) {
         printf("no --ids file; using %d deterministic ids\n", total);
     }
     if (total == 0) { fprintf(stderr, "empty prompt\n"); return 2; }
+    if (debug) { /* layer-0 stage dumps of position 0 from a per-stage GPU pass */
+        refpath *dbg = modpath ? modpath : rp_open(SB_MODEL_QWEN, weights, NULL, ctx);
+        printf("debug: stage dumps of layer 0 at position 0 (%s)\n", rp_module_name(dbg));
+        rp_forward(dbg, ids[0], 0, 0, NULL, 1);
+        if (dbg != modpath) rp_close(dbg);
+    }
     if (selftest > total) selftest = total;
     if (selftest > 0) {
-        float *a = malloc(sizeof(float) * V), *b = malloc(sizeof(float) * V), *tmp = malloc(sizeof(float) * V);
-        sb_engine *d = sb_engine_create(SB_MODEL_QWEN, weights, ctx, SB_FLAG_NO_GRAPH | SB_FLAG_NO_PDL);
-        if (!d) cli_die("engine");
-        for (int p = 0; p < selftest; p++) {
-            if (sb_engine_forward(e, ids[p], p, p == selftest - 1, p == selftest - 1 ? a : NULL)) cli_die("forward");
-            if (sb_engine_forward(d, ids[p], p, p == selftest - 1, p == selftest - 1 ? b : NULL)) cli_die("forward");
-        }
+        printf("selftest: comparing GPU vs serial-CPU logits at position %d...\n", selftest - 1);
+        float *g = malloc(sizeof(float) * V), *c = malloc(sizeof(float) * V), *tmp = malloc(sizeof(float) * V);
+        double ts = cli_now();
+        for (int p = 0; p < selftest; p++) gpu_forward(e, ids[p], p, p == selftest - 1, p == selftest - 1 ? g : NULL);
+        printf("  gpu forward x%d: %.1fs\n", selftest, cli_now() - ts);
+        refpath *cpu = modpath ? modpath : rp_open(SB_MODEL_QWEN, weights, NULL, ctx);
+        ts = cli_now();
+        for (int p = 0; p < selftest; p++)
+            rp_cpu_forward(cpu, ids[p], p, p == selftest - 1, p == selftest - 1 ? c : NULL, debug);
+        printf("  cpu reference x%d: %.1fs\n", selftest, cli_now() - ts);
         double maxerr = 0;
-        for (int i = 0; i < V; i++) maxerr = fmax(maxerr, fabs((double)a[i] - (double)b[i]));
-        int ta[5], tb[5];
-        cli_top5(a, V, ta, tmp);
-        cli_top5(b, V, tb, tmp);
-        printf("selftest at position %d: graph top-5 %d %d %d %d %d | direct top-5 %d %d %d %d %d\n", selftest - 1,
-               ta[0], ta[1], ta[2], ta[3], ta[4], tb[0], tb[1], tb[2], tb[3], tb[4]);
-        printf("  max |graph-direct| logit diff: %.6f  argmax %s\n", maxerr, ta[0] == tb[0] ? "MATCH" : "MISMATCH");
-        printf(ta[0] == tb[0] && maxerr < 1e-3 ? "  SELFTEST: PASS\n" : "  SELFTEST: FAIL\n");
-        sb_engine_destroy(d);
-        free(a); free(b); free(tmp);
+        for (int i = 0; i < V; i++) maxerr = fmax(maxerr, fabs((double)g[i] - (double)c[i]));
+        int tg[5], tc[5];
+        cli_top5(g, V, tg, tmp);
+        cli_top5(c, V, tc, tmp);
+        printf("  gpu top-5 ids: %d %d %d %d %d\n", tg[0], tg[1], tg[2], tg[3], tg[4]);
+        printf("  cpu top-5 ids: %d %d %d %d %d\n", tc[0], tc[1], tc[2], tc[3], tc[4]);
+        printf("  max |gpu-cpu| logit err: %.4f  argmax gpu=%d cpu=%d %s\n", maxerr, tg[0], tc[0],
+               tg[0] == tc[0] ? "MATCH" : "MISMATCH");
+        printf(tg[0] == tc[0] ? "  SELFTEST: PASS\n" : "  SELFTEST: FAIL\n");
+        if (cpu != modpath) rp_close(cpu);
+        free(g); free(c); free(tmp);
     }
     double ts = cli_now();
     int emitted = 0;
     int n = generate(e, ids, total, n_gen, ctx, &emitted);
     double dt = cli_now() - ts;
-    printf("generated %d token(s) in %.3fs -> %.1f tok/s (fp16 weights, 24-layer Qwen2.5-0.5B on B200, %s; "
+    printf("generated %d token(s) in %.3fs -> %.1f tok/s (fp16 weights, 24-layer Qwen2.5-0.5B on B200, %s, %s; "
            "includes priming %d prompt tokens)\n", n - total, dt, (n - total) / dt, greedy_mode ? "greedy" : "sampled",
-           total);
+           modpath ? "per-stage module kernels" : "fused engine", total);
     cli_write_ids("out.ids", ids, n);
     printf("wrote out.ids (%d ids)\n", n);
     printf("ENGINE_DONE\n");
-    sb_engine_destroy(e);
+    if (e) sb_engine_destroy(e);
+    rp_close(modpath);
     return 0;
 }

@@ -92,6 +92,12 @@ def lib():
     _sig(L.sb_attn_decode_noalloc, I, P, P, P, P, I, I, I, I, I, F, P)
     _sig(L.sb_layernorm, I, P, P, P, P, I, F, I, P)
     _sig(L.sb_gelu, I, P, P, I, P)
+    _sig(L.sb_nccl_unique_id, I, P)
+    _sig(L.sb_nccl_comm_init, I, P, I, P, I, ctypes.c_double)
+    _sig(L.sb_nccl_comm_destroy, I, P, ctypes.c_double)
+    _sig(L.sb_nccl_abort, I, P)
+    _sig(L.sb_sgemm_panel_allgather, I, P, P, P, I, I, I, I, I, P, I, P)
+    _sig(L.sb_nccl_wait, I, P, P, ctypes.c_double)
     _sig(L.sb_engine_create, P, I, ctypes.c_char_p, I, ctypes.c_uint)
     _sig(L.sb_engine_destroy, None, P)
     _sig(L.sb_engine_reset, I, P)

@@ -87,3 +87,50 @@ def test_rejects_bad_operands():
         ps(torch.zeros(3, 4), torch.zeros(4, 4))
     with pytest.raises(TypeError):
         ps(torch.zeros(4, 4, dtype=torch.float64), torch.zeros(4, 4, dtype=torch.float64))
+
+
+def _leaver_main(rank, world, port, outdir):
+    """Rank 1 leaves after the first step (between steps, nothing in flight);
+    rank 0's next gather must end with an error within the process group's
+    short timeout instead of waiting for good."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    M, N, K = 16, 8, 4
+    A, B = _operands(M, N, K, 7)
+    ps = sgemm_dist.PanelSgemm(M, N, K, device="cpu", compute=_exact_compute)
+    r0, r1 = sgemm_dist.panel_bounds(M, rank, world)
+    Ap, Bt = torch.from_numpy(A[r0:r1].copy()), torch.from_numpy(B)
+    ps(Ap, Bt)  # step 1: both ranks
+    if rank == 1:
+        os._exit(0)  # leaves without destroying the group
+    t0 = time.time()
+    try:
+        ps(Ap, Bt)  # step 2: the peer is gone
+        outcome = "no error"
+    except Exception as ex:  # gloo reports the closed peer or the timeout
+        outcome = "error: " + type(ex).__name__
+    with open(os.path.join(outdir, "leaver.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.time() - t0:.2f}\n")
+    os._exit(0)
+
+
+def test_rank_leaving_between_steps_fails_fast(tmp_path):
+    """Failure detection on the host: a rank that exits between steps makes
+    the surviving rank's next all-gather raise within the process group's
+    5 s timeout (plus slack), instead of hanging."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver_main, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank was still waiting after 60 s"
+    outcome, secs = (tmp_path / "leaver.txt").read_text().splitlines()[:2]
+    assert outcome.startswith("error"), outcome
+    assert float(secs) < 30.0

@@ -91,3 +91,60 @@ def test_gemv_test_cli(cuda_dev):
     for name in ("gemv", "gemv4", "gemv_warp"):
         assert f"{name}: CORRECT" in out.stdout
     assert out.stdout.rstrip().endswith("GEMV_TEST_DONE")
+
+
+def test_qwen_selftest_and_debug(cuda_dev, qwen_weights, tmp_path):
+    """--selftest N compares the engine's logits at position N-1 with the
+    serial CPU forward written in the host (not the test oracle), as the
+    reference's selftest does; --debug adds the layer-0 stage dumps of
+    position 0 from a per-stage GPU pass (g.*) and from the CPU forward (c.*)."""
+    V = sb200.QWEN["V"]
+    _write_ids(tmp_path / "p.ids", sb200.synth_ids(4, V, 31))
+    out = subprocess.run([os.path.join(BIN, "qwen_engine"), "--weights", str(qwen_weights), "--ids", "p.ids",
+                          "--selftest", "4", "--debug", "--greedy", "--gen", "2", "--ctx", "64"],
+                         capture_output=True, text=True, timeout=600, cwd=tmp_path)
+    assert out.returncode == 0, out.stderr[-800:]
+    o = out.stdout
+    assert "selftest: comparing GPU vs serial-CPU logits at position 3" in o
+    assert "SELFTEST: PASS" in o and "MATCH" in o
+    err = float(o.split("max |gpu-cpu| logit err:")[1].split()[0])
+    assert err < 0.05, o
+    for tag in ("g.ln1", "g.qkv", "g.scores", "g.probs", "g.attnout", "g.res1", "g.gate", "g.swiglu", "g.res2",
+                "c.embed", "c.ln1", "c.qkv", "c.ao", "c.res1"):
+        assert tag in o, tag
+    assert o.rstrip().endswith("ENGINE_DONE")
+
+
+@pytest.mark.parametrize("model", ["qwen", "gpt2"])
+def test_ptx_module_path(cuda_dev, qwen_weights, gpt2_weights, tmp_path, model):
+    """--ptx M decodes through module M's drop-in kernels with the
+    reference's per-stage launches (this package's cubin is passed, as an
+    operator would pass theirs); out.ids equals the oracle's greedy loop."""
+    if model == "qwen":
+        exe, w, V, eos, extra = "qwen_engine", qwen_weights, sb200.QWEN["V"], QW_EOS, ["--greedy", "--ctx", "64"]
+    else:
+        exe, w, V, eos, extra = "gpt2_engine", gpt2_weights, sb200.GPT2["V"], G2_EOS, ["--ctx", "64"]
+    prompt = sb200.synth_ids(6, V, 4242)
+    _write_ids(tmp_path / "p.ids", prompt)
+    mod = sb200.CUBINS[model]
+    out = subprocess.run([os.path.join(BIN, exe), "--weights", str(w), "--ptx", mod, "--ids", "p.ids", "--gen", "6"]
+                         + extra, capture_output=True, text=True, timeout=600, cwd=tmp_path)
+    assert out.returncode == 0, out.stderr[-800:]
+    assert f"module {mod}" in out.stdout and "per-stage module kernels" in out.stdout
+    assert _read_ids(tmp_path / "out.ids") == _oracle_greedy(model, w, V, prompt, 6, eos)
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_gpt2_selftest_trace_ptx(cuda_dev, gpt2_weights, tmp_path, fused):
+    """GPT-2's selftest with the reference's per-layer residual trace of
+    position 0, through --ptx (and --fused: gemv_warp_b launches)."""
+    _write_ids(tmp_path / "p.ids", sb200.synth_ids(5, sb200.GPT2["V"], 55))
+    cmd = [os.path.join(BIN, "gpt2_engine"), "--weights", str(gpt2_weights), "--ptx", sb200.CUBINS["gpt2"], "--ids",
+           "p.ids", "--selftest", "5", "--debug", "--gen", "2", "--ctx", "64"] + (["--fused"] if fused else [])
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=tmp_path)
+    assert out.returncode == 0, out.stderr[-800:]
+    o = out.stdout
+    traces = [ln for ln in o.splitlines() if ln.strip().startswith("trace p0 L")]
+    assert len(traces) == 12
+    assert max(float(ln.split("max|d|=")[1].split()[0]) for ln in traces) < 1e-2
+    assert "SELFTEST: PASS" in o and "g.gelu" in o and "c.gelu" in o
