@@ -58,7 +58,11 @@ int sb_sm_count(void);
 
 /* ---- SGEMM (replaces the launches of gpu_workload.c:90,135,142,160,168,186)
  * C[M][N] = A[M][K] . B[K][N], FP32 row-major, FP32 FFMA on CUDA cores.
- * Any M, N, K >= 0; 128-bit loads when K, N % 4 == 0 and pointers aligned. */
+ * Any M, N, K >= 0; 128-bit loads when K, N % 4 == 0 and pointers aligned.
+ * Products with fewer 128x128 tiles than two per SM (M, N % 128 == 0,
+ * aligned) split K over CTAs through a library-owned workspace and add the
+ * partial tiles in split order (deterministic); split-K calls on different
+ * streams of one context must not overlap. */
 int sb_sgemm(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
 /* Rows [row0, row1) of C only: the row panel a rank computes when C is
  * sharded across GPUs (A, C point at the full matrices). */
@@ -187,6 +191,9 @@ typedef struct sb_engine sb_engine;
                                  * persistent whole-step kernel (both models) */
 #define SB_FLAG_NO_PREFILL 8u /* sb_engine_generate primes the prompt one token
                                * per step instead of sb_engine_prefill        */
+#define SB_FLAG_MK_V1 16u     /* Qwen: the earlier persistent kernel (MLP down
+                               * projection after a hand-off of the whole
+                               * hidden vector) instead of the split-K one  */
 #define SB_GEN_STOP_EOS 1u   /* stop at the model's end tokens (reference behaviour) */
 
 /* max_ctx: KV-cache positions (<= 8192 Qwen, <= 1024 GPT-2). NULL on error. */

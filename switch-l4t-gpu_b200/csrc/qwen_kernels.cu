@@ -524,10 +524,36 @@ extern "C" __global__ void fp16_flush_subnormals(uint4 *__restrict__ p, long n16
     }
 }
 
+// out[z][c][r] = in[z][r][c]: per layer z, an fp16 rows x cols matrix
+// transposed through 32 x 32 shared-memory tiles (both sides coalesced).
+// The engine writes W_down's transpose with it once at load time, for the
+// persistent kernel's split-K down projection.  grid (ceil(cols/32),
+// ceil(rows/32), layers), block 256.
+extern "C" __global__ void __launch_bounds__(256) transpose_u16(const unsigned short *__restrict__ in,
+                                                               unsigned short *__restrict__ out, int rows, int cols,
+                                                               long in_stride, long out_stride) {
+    __shared__ unsigned short t[32][33];
+    if (blockDim.x != 256) return;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    in += blockIdx.z * in_stride;
+    out += blockIdx.z * out_stride;
+    for (int i = ty; i < 32; i += 8) {
+        const int r = r0 + i, c = c0 + tx;
+        if (r < rows && c < cols) t[i][tx] = in[(size_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int c = c0 + i, r = r0 + tx;
+        if (c < cols && r < rows) out[(size_t)c * rows + r] = t[tx][i];
+    }
+}
+
 // =====================================================================
-// Part 3 -- the persistent whole-step kernel
+// Part 3 -- the persistent whole-step kernels
 // =====================================================================
 #include "qwen_mk.cuh"
+#include "qwen_mk2.cuh"
 
 // ===========================================================================
 // Batched prompt prefill: T prompt tokens at positions pos0..pos0+T-1 run

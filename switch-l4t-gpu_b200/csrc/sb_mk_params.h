@@ -10,6 +10,10 @@
  * MLP hidden[4864] | attention partials [14 heads][8 splits][66]. */
 #define SB_MK_LL_WORDS (896 + 1152 + 4864 + 14 * 8 * 66)
 #define SB_MK_SPLITS_MAX 8
+/* qwen_decode_mk2: x (a 16-word line per CTA, up to 160 CTAs) | q k v |
+ * attention partials (80 words each) | down partials [CTA][896] */
+#define SB_MK2_LL_DP (160 * 16 + 1152 + 14 * 8 * 80)
+#define SB_MK2_LL_WORDS(ctas) (SB_MK2_LL_DP + (ctas) * 896)
 
 typedef struct SbMkParams {
     unsigned long long w;      /* weight file image                              */
@@ -30,6 +34,8 @@ typedef struct SbMkParams {
     int test_stall;            /* test hook: 0, or k > 0 -- CTA k-1 withholds its
                                 * layer-0 outputs, so every other CTA's bounded
                                 * wait runs out and the step reports an error */
+    unsigned long long aux;    /* qwen_decode_mk2: W_down transposed per layer,
+                                * [layers][4864][896] fp16                       */
 } SbMkParams;
 
 #endif

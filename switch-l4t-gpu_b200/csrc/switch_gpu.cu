@@ -74,10 +74,13 @@ __device__ __forceinline__ void sg_store_slice(SgSmem &s, int buf, int ams, int 
     *reinterpret_cast<float4 *>(&s.Bs[buf][br][bc]) = rb;
 }
 
+// k range [kbeg, kbeg + klen) of the product (split-K: the unpredicated
+// path only, kbeg and klen multiples of SG_BK); K stays A's row stride.
 template <bool EDGE>
 __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const float *__restrict__ B,
                                             float *__restrict__ C, int M, int N, int K, int tid, int cta,
-                                            int ncta, SgSmem &s) {
+                                            int ncta, SgSmem &s, int kbeg = 0, int klen = -1) {
+    if (klen < 0) klen = K;
     const int warp = tid >> 5, lane = tid & 31;
     const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15
     const int tx = (warp & 1) * 8 + (lane & 7);    // 0..15
@@ -87,7 +90,7 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
     const int ams2 = (((ar >> 2) ^ sg_swz(ak + 8)) << 2) | (ar & 3);
     const int tiles_m = (M + SG_BM - 1) / SG_BM, tiles_n = (N + SG_BN - 1) / SG_BN;
     const int ntiles = tiles_m * tiles_n;
-    const int nk = (K + SG_BK - 1) / SG_BK;
+    const int nk = (klen + SG_BK - 1) / SG_BK;
 
     for (int tile = cta; tile < ntiles; tile += ncta) {
         // grouped raster: 8 tile-rows share the B column panels in L2
@@ -105,8 +108,8 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
             for (int j = 0; j < 4; j++) acc[i][j] = 0ull;
 
         // unpredicated path: running pointers to this thread's A row / B k-row
-        const float *Ap = A + (size_t)(m0 + ar) * K + ak;
-        const float *Bp = B + (size_t)br * N + n0 + bc;
+        const float *Ap = A + (size_t)(m0 + ar) * K + kbeg + ak;
+        const float *Bp = B + (size_t)(kbeg + br) * N + n0 + bc;
         float4 ra, rb, ra2, rb2;
         if (EDGE) {
             sg_load_slice(A, B, M, N, K, m0, n0, 0, ar, ak, br, bc, ra, rb);
@@ -238,6 +241,24 @@ extern "C" __global__ void __launch_bounds__(256, 2)
 extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_b200(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
     sgemm_entry(A, B, C, M, N, K);
+}
+
+// Split-K form for products with fewer 128 x 128 tiles than the GPU has CTA
+// slots (e.g. 1024^3: 64 tiles on 148 SMs): CTA (tile, split) multiplies the
+// tile over k range split and writes it to ws[split][M][N]; the splits are
+// then added in split order (gemm_splitk_reduce), so results are
+// deterministic.  Needs M, N % 128 == 0, K % (16 * splits) == 0 and 16-byte
+// aligned pointers (the host checks).  grid = tiles * splits, block 256.
+extern "C" __global__ void __launch_bounds__(256, 2)
+    sgemm_b200_sk(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ ws, int M, int N, int K,
+                  int splits) {
+    if (blockDim.x * blockDim.y * blockDim.z != SG_THREADS) return;
+    __shared__ __align__(16) SgSmem s;
+    const int tiles = (M / SG_BM) * (N / SG_BN);
+    const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
+    if (tile >= tiles) return;
+    const int klen = K / splits;
+    sgemm_tiles<false>(A, B, ws + (size_t)split * M * N, M, N, K, threadIdx.x, tile, tiles, s, split * klen, klen);
 }
 
 // One output per thread, k in order, product and sum rounded separately:

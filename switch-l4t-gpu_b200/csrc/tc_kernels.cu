@@ -37,6 +37,11 @@ constexpr int A_BYTES = BM * BK * 2;  // 16 KB per W stage
 }  // namespace tck
 
 __device__ int tc_err;  // nonzero after a wait timed out (read and cleared by the host)
+// Failure-detection test hook (set by the host, sb_tc_set_test_skip): k + 1
+// makes every gemm_hh_tc producer stop before issuing its K-chunk k, so the
+// MMA issuer's wait for that stage runs out and the kernel reports tc_err;
+// 0 = off.
+__device__ int tc_test_skip;
 
 namespace tck {
 SB_DEV unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -46,7 +51,20 @@ SB_DEV void mbar_init(uint64_t *mb, unsigned count) {
 SB_DEV void mbar_expect_tx(uint64_t *mb, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(mb)), "r"(bytes) : "memory");
 }
-SB_DEV bool mbar_wait(uint64_t *mb, unsigned ph) {
+SB_DEV unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for phase `ph` of an mbarrier.  Gives up after WAIT_NS of
+// wall time (or SPIN polls), raising tc_err.  `abortable` waits -- for
+// something another role may never deliver once it has stopped -- also
+// return early when another thread already raised tc_err; the others (a
+// TMA copy or MMA batch this CTA issued, which always completes) keep
+// waiting, so a CTA never frees shared or tensor memory under work in flight.
+constexpr unsigned long long WAIT_NS = 2000000000ull;
+SB_DEV bool mbar_wait(uint64_t *mb, unsigned ph, bool abortable = true) {
+    unsigned long long t0 = 0;
     for (long spin = 0; spin < SPIN; spin++) {
         unsigned done;
         asm volatile(
@@ -55,7 +73,12 @@ SB_DEV bool mbar_wait(uint64_t *mb, unsigned ph) {
             : "r"(smem_u32(mb)), "r"(ph)
             : "memory");
         if (done) return true;
-        if ((spin & 1023) == 1023 && *(volatile int *)&tc_err) return false;
+        if ((spin & 1023) == 1023) {
+            if (abortable && *(volatile int *)&tc_err) return false;
+            const unsigned long long t = gtimer();
+            if (t0 == 0) t0 = t;
+            else if (t - t0 > WAIT_NS) break;
+        }
     }
     atomicExch(&tc_err, 1);
     return false;
@@ -153,9 +176,11 @@ extern "C" __global__ void __launch_bounds__(tck::THREADS, 1)
     if (warp == 4 && lane == 0) {
         // ---- TMA producer
         const unsigned tx = (unsigned)(A_BYTES + b_bytes);
+        const int skip = tc_test_skip - 1;  // test hook: -1 = off
         int issued = 0;
         bool ok = true;
         for (int c = c0; c < c1 && ok; c++, issued++) {
+            if (issued == skip) break;  // withhold this stage: the MMA issuer's wait runs out
             const int s = issued % STAGES;
             if (issued >= STAGES) ok = mbar_wait(&empty[s], ((issued / STAGES) - 1) & 1);
             if (!ok) break;
@@ -164,7 +189,8 @@ extern "C" __global__ void __launch_bounds__(tck::THREADS, 1)
             tma_2d(b_st + (size_t)s * b_bytes, &tm_x, c * BK, 0, &full[s]);
         }
         // every stage issued must have landed before this CTA may exit
-        for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++) mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+        for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
+            mbar_wait(&full[i % STAGES], (i / STAGES) & 1, false);
     } else if (warp == 5 && lane == 0) {
         // ---- MMA issuer
         const uint32_t idesc = idesc_f16(n_pad);
@@ -181,8 +207,10 @@ extern "C" __global__ void __launch_bounds__(tck::THREADS, 1)
         }
         mma_commit(accb);  // arrives once every MMA issued above has completed
     } else if (warp < 4) {
-        // ---- epilogue: wait for the accumulator, TMEM -> registers -> global
-        const bool ok = mbar_wait(accb, 0);
+        // ---- epilogue: wait for the accumulator (the MMA issuer always
+        // commits it, also after giving up, once its MMAs have drained),
+        // TMEM -> registers -> global; nothing is stored after a timeout
+        const bool ok = mbar_wait(accb, 0, false) && !*(volatile int *)&tc_err;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int n = m0 + warp * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
@@ -297,6 +325,7 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
     uint64_t *full = bars, *conv = bars + STAGES, *empty = bars + 2 * STAGES;
     uint64_t *acc_full = bars + 3 * STAGES, *acc_empty = acc_full + NACC;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + NACC);
+    uint64_t *fin = acc_empty + NACC + 1;  // the MMA issuer's last commit
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_n = (N + BN - 1) / BN;
     const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
@@ -315,6 +344,7 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
             tck::mbar_init(&acc_full[q], 1);
             tck::mbar_init(&acc_empty[q], 128);
         }
+        tck::mbar_init(fin, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -340,7 +370,7 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
                 tck::tma_2d(st + TILE, &tm_bt, (kt0 + kt) * BK, n0, &full[s]);
             }
             for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; i++)
-                tck::mbar_wait(&full[i % STAGES], (i / STAGES) & 1);
+                tck::mbar_wait(&full[i % STAGES], (i / STAGES) & 1, false);
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
@@ -364,6 +394,9 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
                 tck::mma_commit(&empty[s]);
                 if (kt % CHUNK == CHUNK - 1 || kt == nk - 1) tck::mma_commit(&acc_full[q]);
             }
+            // no MMA may still write tensor memory when it is freed below
+            tck::mma_commit(fin);
+            tck::mbar_wait(fin, 0, false);
         }
     } else {
         // ---- warps 2-5: split each stage into big/small, promote finished

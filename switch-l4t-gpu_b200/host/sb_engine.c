@@ -45,8 +45,10 @@ struct sb_engine {
     int V, NL, kvw;
     CUgraphExec gexec[2];
     int n_prompt, n_end;
-    /* persistent whole-step kernel (qwen_decode_mk / gpt2_decode_mk) */
-    int mk;
+    /* persistent whole-step kernel (qwen_decode_mk2 / qwen_decode_mk / gpt2_decode_mk) */
+    int mk, mk2;
+    CUdeviceptr wdt; /* mk2: W_down transposed per layer [NL][FC][C] fp16 */
+    size_t ll_words;
     CUdeviceptr ll, sync, err; /* flagged exchange words; u32[2] seq / arrivals; error flag */
     int mk_splits, mk_score_cap;
     unsigned mk_smem;
@@ -69,6 +71,15 @@ static unsigned mk_smem_bytes(int model, int score_cap) {
                                                  : G2_FC * 4 + MK_WARPS * (3 * G2_C * 4 + G2_C * 2);
     const unsigned hl = model == SB_MODEL_QWEN ? QW_C * 4 : 0; /* fp16 hi / lo activation vectors */
     return head + (unsigned)score_cap * 4 + (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4 + hl;
+}
+
+/* qwen_decode_mk2: warp regions of 5 rows + an O half-row, the CTA's W_downT
+ * rows (ceil(FC / CTAs) of them), scores, the attention scratch and the fp16
+ * hi / lo activation vectors */
+static unsigned mk2_smem_bytes(int score_cap, int ctas) {
+    const unsigned dsmax = (unsigned)CEIL_DIV(QW_FC, ctas);
+    return MK_WARPS * (5 * QW_C * 2 + QW_C) + dsmax * QW_C * 2 + (unsigned)((score_cap + 3) & ~3) * 4 +
+           (32 + MK_WARPS * 64 + MK_WARPS + QW_NH * SB_MK_SPLITS_MAX * 2) * 4 + QW_C * 4;
 }
 
 /* ------------------------------------------------------------------ upload */
@@ -227,7 +238,7 @@ static int launch_kernel(sb_engine *e, int l, int which, int with_logits, int pd
                                      : launch_gpt2(e, l, which, with_logits, pdl);
 }
 
-static int mk_fn(int model) { return model == SB_MODEL_QWEN ? F_QWEN_MK : F_GPT2_MK; }
+static int mk_fn(int model, int v2) { return model == SB_MODEL_QWEN ? (v2 ? F_QWEN_MK2 : F_QWEN_MK) : F_GPT2_MK; }
 
 static int record_mk(sb_engine *e, int with_logits) {
     SbMkParams prm;
@@ -246,8 +257,10 @@ static int record_mk(sb_engine *e, int with_logits) {
     prm.splits = e->mk_splits;
     prm.score_cap = e->mk_score_cap;
     prm.test_stall = e->test_stall;
+    prm.aux = e->wdt;
     void *args[] = {&prm};
-    return sb_launch_coop(e->c, mk_fn(e->model), (unsigned)e->c->sms, MK_THREADS, e->mk_smem, e->stream, args);
+    return sb_launch_coop(e->c, mk_fn(e->model, e->mk2), (unsigned)e->c->sms, MK_THREADS, e->mk_smem, e->stream,
+                          args);
 }
 
 static int record_model(sb_engine *e, int with_logits) {
@@ -320,11 +333,17 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
         e->mk_splits = c->sms / (model == SB_MODEL_QWEN ? QW_NH : G2_NH);
         if (e->mk_splits > SB_MK_SPLITS_MAX) e->mk_splits = SB_MK_SPLITS_MAX;
         e->mk_score_cap = (CEIL_DIV(max_ctx, e->mk_splits) + 8 + 3) & ~3; /* multiple of 4 floats */
-        e->mk_smem = mk_smem_bytes(model, e->mk_score_cap);
         int coop = 0;
         cuDeviceGetAttribute(&coop, CU_DEVICE_ATTRIBUTE_COOPERATIVE_LAUNCH, c->dev);
-        e->mk = coop && sb_occupancy(c, mk_fn(model), MK_THREADS, e->mk_smem) >= 1;
+        /* Qwen: the split-K kernel unless asked for the earlier one (or it does not fit) */
+        if (model == SB_MODEL_QWEN && !(flags & SB_FLAG_MK_V1) && c->sms <= 160) {
+            e->mk_smem = mk2_smem_bytes(e->mk_score_cap, c->sms);
+            e->mk2 = coop && sb_occupancy(c, F_QWEN_MK2, MK_THREADS, e->mk_smem) >= 1;
+        }
+        if (!e->mk2) e->mk_smem = mk_smem_bytes(model, e->mk_score_cap);
+        e->mk = e->mk2 || (coop && sb_occupancy(c, mk_fn(model, 0), MK_THREADS, e->mk_smem) >= 1);
     }
+    e->ll_words = e->mk2 ? (size_t)SB_MK2_LL_WORDS(c->sms) : (size_t)SB_MK_LL_WORDS;
     const int groups = qw ? QW_NKV : G2_NH, G = qw ? QW_NH / QW_NKV : 1;
     const int C = qw ? QW_C : G2_C, FC = qw ? QW_FC : G2_FC, NQ = qw ? QW_C : G2_C;
 
@@ -342,6 +361,20 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
             if (sb_launch(c, F_FP16_FLUSH, 4 * c->sms, 1, 256, 0, e->stream, a, 0)) goto fail;
         }
         if (cuStreamSynchronize(e->stream)) { sb_fail(SB_ERR_STATE, "weight flush", __FILE__, __LINE__); goto fail; }
+        if (e->mk2) { /* W_downT [layer][FC][C]: W_down [C][FC] of every layer, transposed (flushed above) */
+            const size_t bytes = (size_t)QW_NL * QW_FC * QW_C * 2;
+            if (cuMemAlloc(&e->wdt, bytes)) { sb_fail(SB_ERR_STATE, "W_downT allocation", __FILE__, __LINE__); goto fail; }
+            CUdeviceptr src = e->w + QW_LBASE + QWL_DOWN * 2, dst = e->wdt;
+            int rows = QW_C, cols = QW_FC;
+            long in_stride = (long)(QW_LSTRIDE / 2), out_stride = (long)QW_FC * QW_C;
+            void *a[] = {&src, &dst, &rows, &cols, &in_stride, &out_stride};
+            CUstream s = e->stream;
+            if (sb_launch3(c, F_TRANSPOSE_U16, CEIL_DIV(QW_FC, 32), CEIL_DIV(QW_C, 32), QW_NL, 256, s, a) ||
+                cuStreamSynchronize(s)) {
+                sb_fail(SB_ERR_STATE, "W_downT transpose", __FILE__, __LINE__);
+                goto fail;
+            }
+        }
     }
     const size_t kv_bytes = (size_t)2 * e->NL * max_ctx * e->kvw * 4;
     if (cuMemAlloc(&e->kv, kv_bytes)) { sb_fail(SB_ERR_STATE, "KV allocation", __FILE__, __LINE__); goto fail; }
@@ -361,7 +394,7 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     CARVE(counters, groups * 4);
     CARVE(step, sizeof(SbStep));
     CARVE(tokens, (size_t)(max_ctx + 2) * 4);
-    CARVE(ll, (size_t)SB_MK_LL_WORDS * 8);
+    CARVE(ll, e->ll_words * 8);
     CARVE(sync, 8);
     CARVE(err, 4);
 #undef CARVE
@@ -392,6 +425,7 @@ void sb_engine_destroy(sb_engine *e) {
     for (int i = 0; i < 2; i++)
         if (e->gexec[i]) cuGraphExecDestroy(e->gexec[i]);
     if (e->scratch) cuMemFree(e->scratch);
+    if (e->wdt) cuMemFree(e->wdt);
     if (e->kv) cuMemFree(e->kv);
     if (e->w) cuMemFree(e->w);
     if (e->stream) cuStreamDestroy(e->stream);
@@ -446,7 +480,7 @@ double sb_engine_step_bytes(sb_engine *e) {
  * returned early instead of hanging); report it and clear the flag. */
 /* Clear the flagged words and the sequence number (epoch 0 never matches). */
 static int mk_clear_words(sb_engine *e) {
-    SB_CK(cuMemsetD8Async(e->ll, 0, (size_t)SB_MK_LL_WORDS * 8, e->stream));
+    SB_CK(cuMemsetD8Async(e->ll, 0, e->ll_words * 8, e->stream));
     SB_CK(cuMemsetD32Async(e->sync, 0, 2, e->stream));
     e->mk_steps = 0;
     return 0;

@@ -15,6 +15,7 @@ enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_TC, M_COUNT };
 
 typedef enum {
     F_SGEMM_B200 = 0,
+    F_SGEMM_B200_SK,
     F_SGEMM_NAIVE,
     F_MEMBW,
     F_FMA_PEAK,
@@ -51,6 +52,8 @@ typedef enum {
     F_QWEN_LMHEAD,
     F_QWEN_FINALIZE,
     F_QWEN_MK,
+    F_QWEN_MK2,
+    F_TRANSPOSE_U16,
     F_FP16_FLUSH,
     F_GEMM_HH_TC,
     F_SPLITK_REDUCE,
@@ -106,6 +109,7 @@ int sb_launch(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned bx, unsi
               void **args, int pdl);
 /* cooperative launch (all CTAs co-resident, required by grid-wide barriers) */
 int sb_launch_coop(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned bx, unsigned smem, CUstream s, void **args);
+int sb_launch3(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned gz, unsigned bx, CUstream s, void **args);
 /* max co-resident CTAs of f per SM at this block size / dynamic smem */
 int sb_occupancy(sb_ctx *c, sb_fn_id f, int block, size_t smem);
 

@@ -10,7 +10,31 @@
 #define ALIGNED16(p) ((((uintptr_t)(p)) & 15) == 0)
 
 
+/* The library-owned split-K workspace of this context (grown on demand;
+ * shared by every split-K product, which run in order on their streams). */
+static int ws_reserve(sb_ctx *c, size_t need, CUdeviceptr *ws) {
+    if (c->tc_ws_bytes < need) {
+        if (c->tc_ws) cuMemFree(c->tc_ws);
+        c->tc_ws = 0;
+        c->tc_ws_bytes = 0;
+        SB_CK(cuMemAlloc(&c->tc_ws, need));
+        c->tc_ws_bytes = need;
+    }
+    *ws = c->tc_ws;
+    return 0;
+}
+
 /* ------------------------------------------------------------------ SGEMM */
+/* Split-K count for a product of `tiles` 128x128 tiles: enough CTAs to fill
+ * two per SM, each still running at least 8 k-slices of 16; 1 = no split. */
+static int sgemm_splits(const sb_ctx *c, long tiles, int M, int N, int K, const void *A, const void *B,
+                        const void *C) {
+    if (M % 128 || N % 128 || !ALIGNED16(A) || !ALIGNED16(B) || !ALIGNED16(C)) return 1;
+    int s = (int)((2L * c->sms) / (tiles > 0 ? tiles : 1));
+    while (s > 1 && (K % (16 * s) || K / s < 128)) s--;
+    return s < 1 ? 1 : s;
+}
+
 int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
                   void *stream) {
     SB_ARG(M >= 0 && N >= 0 && K >= 0 && 0 <= row0 && row0 <= row1 && row1 <= M, "bad SGEMM shape");
@@ -23,6 +47,23 @@ int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K,
     /* one CTA per 128x128 tile (two resident per SM); the kernel's tile loop
      * covers the rest if the count ever exceeds the grid limit */
     const long tiles = (long)CEIL_DIV(m, 128) * CEIL_DIV(N, 128);
+    const int splits = tiles < c->sms ? sgemm_splits(c, tiles, m, N, K, (const void *)(uintptr_t)a, B,
+                                                     (const void *)(uintptr_t)cc)
+                                      : 1;
+    if (splits > 1) { /* small products: k split over CTAs, partial tiles added in split order */
+        CUdeviceptr ws;
+        int rc = ws_reserve(c, (size_t)splits * m * N * 4, &ws);
+        if (rc) return rc;
+        void *args[] = {&a, &b, &ws, (void *)&m, &N, &K, (void *)&splits};
+        rc = sb_launch(c, F_SGEMM_B200_SK, (unsigned)(tiles * splits), 1, 256, 0, (CUstream)stream, args, 0);
+        if (rc) return rc;
+        long total = (long)m * N;
+        int sp = splits;
+        void *rargs[] = {&ws, &cc, &total, &sp};
+        long g = CEIL_DIV(total, 256 * 4);
+        if (g > 8L * c->sms) g = 8L * c->sms;
+        return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
+    }
     const long grid = tiles < 0x7fffffffL ? tiles : 0x7fffffffL;
     void *args[] = {&a, &b, &cc, (void *)&m, &N, &K};
     return sb_launch(c, F_SGEMM_B200, (unsigned)grid, 1, 256, 0, (CUstream)stream, args, 0);

@@ -34,6 +34,7 @@ static const struct {
     const char *name;
 } fn_table[F_COUNT] = {
     [F_SGEMM_B200] = {M_SWITCH, "sgemm_b200"},
+    [F_SGEMM_B200_SK] = {M_SWITCH, "sgemm_b200_sk"},
     [F_SGEMM_NAIVE] = {M_SWITCH, "sgemm_naive"},
     [F_MEMBW] = {M_SWITCH, "membw_read4"},
     [F_FMA_PEAK] = {M_SWITCH, "fma_peak"},
@@ -70,6 +71,8 @@ static const struct {
     [F_QWEN_LMHEAD] = {M_QWEN, "qwen_lmhead"},
     [F_QWEN_FINALIZE] = {M_QWEN, "sb_finalize"},
     [F_QWEN_MK] = {M_QWEN, "qwen_decode_mk"},
+    [F_QWEN_MK2] = {M_QWEN, "qwen_decode_mk2"},
+    [F_TRANSPOSE_U16] = {M_QWEN, "transpose_u16"},
     [F_FP16_FLUSH] = {M_QWEN, "fp16_flush_subnormals"},
     [F_GEMM_HH_TC] = {M_TC, "gemm_hh_tc"},
     [F_SPLITK_REDUCE] = {M_TC, "gemm_splitk_reduce"},
@@ -211,6 +214,14 @@ int sb_launch(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned bx, unsi
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     SB_CK(cuLaunchKernelEx(&cfg, c->fn[f], args, NULL));
+    return 0;
+}
+
+/* plain launch on a 3-D grid (no dynamic shared memory, no PDL) */
+int sb_launch3(sb_ctx *c, sb_fn_id f, unsigned gx, unsigned gy, unsigned gz, unsigned bx, CUstream s, void **args) {
+    if (!c->fn[f]) SB_CK(cuModuleGetFunction(&c->fn[f], c->mod[fn_table[f].mod], fn_table[f].name));
+    if (gx == 0 || gy == 0 || gz == 0) return 0;
+    SB_CK(cuLaunchKernel(c->fn[f], gx, gy, gz, bx, 1, 1, 0, s, args, NULL));
     return 0;
 }
 

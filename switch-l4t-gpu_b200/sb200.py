@@ -25,6 +25,7 @@ FLAG_NO_GRAPH = 1
 FLAG_NO_PDL = 2
 FLAG_MULTI_KERNEL = 4
 FLAG_NO_PREFILL = 8
+FLAG_MK_V1 = 16  # Qwen: the earlier persistent step kernel (A/B and regression tests)
 GEN_STOP_EOS = 1
 
 QWEN = dict(V=151936, C=896, NL=24, NH=14, NKV=2, HD=64, FC=4864, CTX_FILE=8192,

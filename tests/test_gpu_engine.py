@@ -37,9 +37,11 @@ def _teacher_forced(model_id, weights, vocab, ctx, ids, flags=0):
         ref.close()
 
 
-@pytest.mark.parametrize("flags", [0, sb200.FLAG_MULTI_KERNEL])
+@pytest.mark.parametrize("flags", [0, sb200.FLAG_MK_V1, sb200.FLAG_MULTI_KERNEL])
 def test_qwen_teacher_forced(cuda_dev, qwen_weights, flags):
-    """flags 0: the persistent whole-step kernel; MULTI_KERNEL: one kernel per stage."""
+    """flags 0: the persistent whole-step kernel (split-K MLP down
+    projection); MK_V1: the earlier persistent kernel; MULTI_KERNEL: one
+    kernel per stage."""
     ids = sb200.synth_ids(12, sb200.QWEN["V"], 7)
     _teacher_forced(sb200.MODEL_QWEN, qwen_weights, sb200.QWEN["V"], 64, ids, flags)
 
