@@ -505,7 +505,7 @@ def gpt2_section(torch, dev, dist, steps, warmup, with_cpu):
     tok_ms = total_ms / (steps * GPT2_GEN)
     step_bytes = eng.step_bytes()
     achieved = step_bytes / (tok_ms * 1e-3) / 1e9
-    dom = "gpt2_decode_mk" if eng.persistent else "gpt2 per-stage kernels"
+    dom = eng.step_kernel
     out = {
         "metric": "GPT-2-124M-shape FP32 decode tok/s", "value": round(value, 2), "unit": UNIT,
         "ms_per_step": round(total_ms / steps, 3), "steps": steps, "dtype": "f32",
@@ -760,7 +760,7 @@ def run_b200(args):
     step_bytes = eng.step_bytes()
     tok_ms = total_ms / (args.steps * N_GEN)
     if eng.persistent:
-        dom, dbytes, dms = "qwen_decode_mk", step_bytes, tok_ms
+        dom, dbytes, dms = eng.step_kernel, step_bytes, tok_ms
         kernels = {}
     else:
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)

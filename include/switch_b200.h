@@ -69,6 +69,13 @@ int sb_sgemm(const float *A, const float *B, float *C, int M, int N, int K, void
 int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
                   void *stream);
 
+/* The same CUDA-core SGEMM with its operand tiles staged by TMA
+ * (cp.async.bulk.tensor into a 4-stage shared-memory ring, persistent CTAs,
+ * a producer warp and eight compute warps): bit-identical to sb_sgemm (each
+ * output one fma chain over k in order).  K % 4 == 0, N % 4 == 0, 16-byte
+ * aligned pointers; any M, N.  No counterpart in the reference. */
+int sb_sgemm_tma(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
+
 /* ---- multi-GPU SGEMM (row panels + NCCL all-gather of C), one rank per GPU.
  * No counterpart in the reference, which runs on device 0 only
  * (gpu_workload.c:66-67).  NCCL is loaded at run time (libnccl.so.2).
@@ -129,8 +136,11 @@ int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
  * and prefill form of gemv_h.  fp16 subnormals are used as subnormals (the
  * tensor pipe does not flush them).  K % 8 == 0; W, X 16-byte aligned.
  * Short matrices are split along K through a library-owned workspace and
- * summed in split order, so results are deterministic.  No counterpart in
- * the reference (its prefill is gemv_multi, gpt2_kernels.cu:115-155). */
+ * summed in split order, so results are deterministic; batches of up to 16
+ * rows on short outputs (fewer than 8 rows per SM) run on the CUDA cores
+ * instead (the mixed-precision FMA, subnormals kept likewise, one launch per
+ * 16 rows).  No counterpart in the reference (its prefill is gemv_multi,
+ * gpt2_kernels.cu:115-155). */
 int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
 /* Opt-in SGEMM on the TF32 tensor pipe with the 3xTF32 split (big/small
  * parts of each operand, three products accumulated in FP32): the contract
@@ -145,6 +155,13 @@ int sb_sgemm_nt_3xtf32(const float *A, const float *Bt, float *C, int M, int N, 
 /* Reads and clears the tensor-core kernels' device error flag (nonzero after
  * a bounded wait gave up); synchronises the context first. */
 int sb_tc_error(int *err);
+/* Failure-detection test hook (no counterpart in the reference): chunk >= 0
+ * makes every later sb_gemm_hh launch's TMA producer stop before its K-chunk
+ * `chunk` (64 k), so the MMA issuer's bounded wait for that stage runs out
+ * (~2 s), the kernel drains what it issued, frees its tensor memory and
+ * returns with the error flag set (sb_tc_error reports it); -1 turns it off.
+ * Synchronises the context first. */
+int sb_tc_set_test_skip(int chunk);
 
 /* ---- decode-step pieces (Qwen2.5 FP16-weight path, qwen_engine.c:205-269)
  * Exposed for kernel-level parity tests; the engines below fuse them.      */
@@ -242,6 +259,9 @@ int sb_engine_launches_per_step(sb_engine *e, int with_logits);
  * SMs: one cooperative launch per token, stages handed over through flagged
  * exchange words), 0 for one kernel per stage. */
 int sb_engine_uses_persistent_kernel(sb_engine *e);
+/* Name of the kernel that runs the decode step ("qwen_decode_mk2",
+ * "qwen_decode_mk", "gpt2_decode_mk", or "<model> per-stage kernels"). */
+const char *sb_engine_step_kernel(sb_engine *e);
 /* Profiling aid for the persistent kernel: dev_buf (u64[SMs][256], or NULL
  * to stop) receives %globaltimer stamps per CTA: [cta][0] = kernel start,
  * [cta][1 + 2k] / [cta][2 + 2k] = inputs ready / outputs written of stage

@@ -235,10 +235,13 @@ extern "C" __global__ void __launch_bounds__(256) gemv_hh4(const unsigned short 
 // global memory (L1-cached, shared by the CTAs of an SM) and flushed per
 // use, so there is no staging round trip.  Warp partials are added in
 // warp order in shared memory.  Block 256.
-template <int B>
+// KEEP: fp16 subnormals of W and X used as subnormals (the tensor pipe's
+// semantics, for sb_gemm_hh's small batches) instead of the reference's
+// flush to zero.  Fewer k-chunks in flight for wide batches (registers).
+template <int B, bool KEEP = false>
 __device__ void gemv_hh_sk_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
                                 float *__restrict__ Y, int K, int N) {
-    constexpr int R = 4, NW = 8, U = 4;
+    constexpr int R = 4, NW = 8, U = B <= 4 ? 4 : (B <= 8 ? 2 : 1);
     __shared__ float part[NW][R * B];
     const int cpr = K / 8, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int per = (cpr + NW - 1) / NW;
@@ -270,10 +273,15 @@ __device__ void gemv_hh_sk_body(const unsigned short *__restrict__ W, const unsi
 #pragma unroll
                     for (int b = 0; b < B; b++) {
                         const uint4 v = __ldg(X4 + (long)b * cpr + c);
-                        const uint4 x = make_uint4(ftz_half2_bits(v.x), ftz_half2_bits(v.y), ftz_half2_bits(v.z),
-                                                   ftz_half2_bits(v.w));
+                        if (KEEP) {
 #pragma unroll
-                        for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh(w[u][r], x, acc[r][b]);
+                            for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh_keep(w[u][r], v, acc[r][b]);
+                        } else {
+                            const uint4 x = make_uint4(ftz_half2_bits(v.x), ftz_half2_bits(v.y), ftz_half2_bits(v.z),
+                                                       ftz_half2_bits(v.w));
+#pragma unroll
+                            for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh(w[u][r], x, acc[r][b]);
+                        }
                     }
                 }
             }
@@ -307,6 +315,31 @@ extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk2(const unsigned sho
 extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk4(const unsigned short *W, const unsigned short *X,
                                                               float *Y, int K, int N) {
     gemv_hh_sk_body<4>(W, X, Y, K, N);
+}
+
+// sb_gemm_hh's small batches (B <= 16) on short outputs, where the tensor
+// cores would split K and add a second launch: the split-K CUDA-core form
+// with subnormals kept (the tensor pipe's semantics), B activation rows per
+// launch.
+extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc1(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<1, true>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc2(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<2, true>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc4(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<4, true>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc8(const unsigned short *W, const unsigned short *X,
+                                                              float *Y, int K, int N) {
+    gemv_hh_sk_body<8, true>(W, X, Y, K, N);
+}
+extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc16(const unsigned short *W, const unsigned short *X,
+                                                               float *Y, int K, int N) {
+    gemv_hh_sk_body<16, true>(W, X, Y, K, N);
 }
 
 // GQA decode attention with an explicit T (no step state); 7 query heads

@@ -378,13 +378,16 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             if (prefetcher) prefetch_piece(l + 1, 1);
         };
         if (!has_item) issue_s3_s4();
-        // ================= S2: attention partials (as qwen_decode_mk)
+        // ================= S2: attention partials; a warp per position, K and V
+        // rows loaded together so one round trip serves scores and P.V.  Each
+        // warp keeps its own softmax (max, sum, P.V) and the CTA combines the
+        // sixteen of them once: two barriers per item.
         const unsigned e_qkv = epoch(l, 0);
         for (int item = b; item < NH * nsplit; item += G) {
             const int h = item / nsplit, s = item % nsplit, g = h / (NH / NKV);
             const int t0 = s * slen, t1 = min(T, t0 + slen), n = max(0, t1 - t0);
             const u64 *kcur = llqkv + C + g * HD + 2 * lane, *vcur = llqkv + C + KVD + g * HD + 2 * lane;
-            __syncthreads();
+            if (item != b) __syncthreads();  // a later item: the previous one's readers are done
             float2 kk[4], vv[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
@@ -397,8 +400,9 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             }
             // warps 0, 1, 2 wait for q_h, the current k, the current v at once
             // (one poller per quantity: all sixteen warps on the same hot
-            // words slowed their producers' stores)
-            float2 *qkv_s = reinterpret_cast<float2 *>(opart);
+            // words slowed their producers' stores).  The hi / lo activation
+            // planes are free during this stage and hold them.
+            float2 *qkv_s = reinterpret_cast<float2 *>(xh4);
             bool ok = true;
             if (warp == 0 || (t1 == T && warp < 3)) {
                 const u64 *src = warp == 0 ? llqkv + h * HD + 2 * lane : (warp == 1 ? kcur : vcur);
@@ -421,6 +425,8 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
                 sc[k] = -1e30f;
                 if (warp + WARPS * k < n) sc[k] = warp_sum(fmaf(q2.x, kk[k].x, q2.y * kk[k].y)) * 0.125f;
             }
+            // positions beyond 64 per item (long contexts): scores via smem, V
+            // re-read (the current position's V word is kept from here)
             float2 vpos = make_float2(0.f, 0.f);
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) {
                 const int t = t0 + j;
@@ -437,17 +443,12 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             float wm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
             __syncwarp();
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) wm = fmaxf(wm, scores[j]);
-            if (lane == 0) wmax_s[warp] = wm;
-            if (__syncthreads_or(!ok)) { aborted = true; break; }
-            float m = -1e30f;
-#pragma unroll
-            for (int w = 0; w < WARPS; w++) m = fmaxf(m, wmax_s[w]);
             float lsum = 0.f;
             float2 o = make_float2(0.f, 0.f);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 if (warp + WARPS * k < n) {
-                    const float e = expf(sc[k] - m);
+                    const float e = expf(sc[k] - wm);
                     lsum += e;
                     o.x = fmaf(e, vv[k].x, o.x);
                     o.y = fmaf(e, vv[k].y, o.y);
@@ -455,7 +456,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             }
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) {
                 const int t = t0 + j;
-                const float e = expf(scores[j] - m);
+                const float e = expf(scores[j] - wm);
                 lsum += e;
                 const float2 v2 = t == pos ? vpos
                                            : __ldcg(reinterpret_cast<const float2 *>(vc + (long)t * KVD + g * HD) + lane);
@@ -463,24 +464,30 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
                 o.y = fmaf(e, v2.y, o.y);
             }
             reinterpret_cast<float2 *>(opart + warp * HD)[lane] = o;
-            if (lane == 0) ksum[warp] = lsum;
+            if (lane == 0) {
+                ksum[warp] = lsum;
+                wmax_s[warp] = wm;
+            }
             __syncthreads();
-            if (tid < HD) {
-                float acc = 0.f;
+            if (tid < HD) {  // the sixteen warp softmaxes combined: partial (o, m, l) of this item
+                float M = -1e30f;
 #pragma unroll
-                for (int w = 0; w < WARPS; w++) acc += opart[w * HD + tid];
+                for (int w = 0; w < WARPS; w++) M = fmaxf(M, wmax_s[w]);
+                float acc = 0.f, ls = 0.f;
+#pragma unroll
+                for (int w = 0; w < WARPS; w++) {
+                    const float f = expf(wmax_s[w] - M);
+                    acc = fmaf(f, opart[w * HD + tid], acc);
+                    ls = fmaf(f, ksum[w], ls);
+                }
                 u64 *pw = llpart + (long)(h * SPLITS_MAX + s) * PW;
                 const unsigned e = epoch(l, 1);
                 ll_put(pw + tid, acc, e);
                 if (tid == 0) {
-                    float ls = 0.f;
-#pragma unroll
-                    for (int w = 0; w < WARPS; w++) ls += ksum[w];
-                    ll_put(pw + HD, m, e);
+                    ll_put(pw + HD, M, e);
                     ll_put(pw + HD + 1, ls, e);
                 }
             }
-            __syncthreads();
         }
         if (aborted) break;
         stamp(l, 1, 1);

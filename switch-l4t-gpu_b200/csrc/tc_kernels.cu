@@ -492,3 +492,149 @@ extern "C" __global__ void __launch_bounds__(256) transpose_f32(const float *__r
         if (c < cols && r < rows) out[(size_t)c * rows + r] = t[tx][i];
     }
 }
+
+// ---------------------------------------------------------------------------
+// sgemm_tma: the FP32 CUDA-core SGEMM (C = A.B row-major, the contract of the
+// reference's sgemm kernels, switch_gpu.cu:5-39) with its operand tiles
+// staged by TMA instead of by the threads:
+//   * persistent CTAs (one per SM), 288 threads: warp 8 lane 0 is the TMA
+//     producer, warps 0-7 (256 threads) compute 128 x 128 tiles, 8 x 8
+//     outputs per thread as packed fma.rn.f32x2;
+//   * a 4-stage ring of 32-deep k-slices: A box {32 k, 128 rows} with the
+//     128-byte swizzle (rows 128 B: chunk c of row r lands at c ^ (r & 7)),
+//     B box {128 n, 32 k} dense; full[s] mbarriers with transaction counts,
+//     empty[s] released by one lane of each compute warp;
+//   * a thread owns rows ty + 16 i (i < 8) -- so the four ty of a warp hit
+//     four different swizzled chunks (no bank conflicts) -- and columns
+//     tx * 4 .. + 3 and 64 + tx * 4 .. + 3; it reads A four k at a time
+//     (one 128-bit load per row) and B one k-row at a time;
+//   * every output is one fma.rn chain over k in order, as in sgemm_b200, so
+//     the two kernels give bit-identical results; TMA zero-fills outside
+//     the matrices (any M, N; K % 4 == 0 and N % 4 == 0 for the 16-byte
+//     strides).
+// The threads no longer load, transpose and store the tiles, so their issue
+// slots go to the FMAs.
+namespace sgt {
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 4, THREADS = 288;
+constexpr int A_BYTES = BM * BK * 4, B_BYTES = BK * BN * 4, STAGE = A_BYTES + B_BYTES;
+SB_DEV void mbar_arrive(uint64_t *mb) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tck::smem_u32(mb)) : "memory");
+}
+}  // namespace sgt
+
+// grid: min(tiles, SMs) CTAs; block sgt::THREADS; dynamic smem 1024 + STAGES * STAGE + 128.
+extern "C" __global__ void __launch_bounds__(sgt::THREADS, 1)
+    sgemm_tma(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, float *__restrict__ C,
+              int M, int N, int K) {
+    using namespace sgt;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE), *empty = full + STAGES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN, ntiles = tiles_m * tiles_n;
+    const int nk = (K + BK - 1) / BK;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            tck::mbar_init(&full[s], 1);
+            tck::mbar_init(&empty[s], 8);  // one lane of each compute warp
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    // grouped raster (8 tile-rows share B's column panels in L2), as sgemm_b200
+    auto tile_mn = [=](int tile) {
+        const int per_group = 8 * tiles_n, first_m = (tile / per_group) * 8;
+        const int gsz = min(tiles_m - first_m, 8);
+        return make_int2((first_m + (tile % per_group) % gsz) * BM, ((tile % per_group) / gsz) * BN);
+    };
+    if (warp == 8) {
+        if (lane == 0) {  // ---- TMA producer
+            long it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                const int2 mn = tile_mn(tile);
+                const int m0 = mn.x, n0 = mn.y;
+                for (int kt = 0; kt < nk; kt++, it++) {
+                    const int s = (int)(it % STAGES);
+                    if (it >= STAGES && !(ok = tck::mbar_wait(&empty[s], (unsigned)(((it / STAGES) - 1) & 1)))) break;
+                    unsigned char *st = smem + (size_t)s * STAGE;
+                    tck::mbar_expect_tx(&full[s], STAGE);
+                    tck::tma_2d(st, &tm_a, kt * BK, m0, &full[s]);
+                    tck::tma_2d(st + A_BYTES, &tm_b, n0, kt * BK, &full[s]);
+                }
+            }
+            // every stage issued must have landed before this CTA may exit
+            for (long i = (it > STAGES ? it - STAGES : 0); i < it; i++)
+                tck::mbar_wait(&full[i % STAGES], (unsigned)((i / STAGES) & 1), false);
+        }
+        return;
+    }
+    // ---- warps 0-7: compute
+    const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15
+    const int tx = (warp & 1) * 8 + (lane & 7);    // 0..15
+    long it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int2 mn = tile_mn(tile);
+        const int m0 = mn.x, n0 = mn.y;
+        unsigned long long acc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] = 0ull;
+        for (int kt = 0; kt < nk; kt++, it++) {
+            const int s = (int)(it % STAGES);
+            if (!(ok = tck::mbar_wait(&full[s], (unsigned)((it / STAGES) & 1)))) break;
+            const float *As = reinterpret_cast<const float *>(smem + (size_t)s * STAGE);
+            const float *Bs = reinterpret_cast<const float *>(smem + (size_t)s * STAGE + A_BYTES);
+#pragma unroll 1
+            for (int kq = 0; kq < BK / 4; kq++) {
+                float4 a[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int r = ty + 16 * i;
+                    a[i] = *reinterpret_cast<const float4 *>(As + r * BK + ((kq ^ (r & 7)) << 2));
+                }
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const float *brow = Bs + (kq * 4 + kk) * BN;
+                    const float4 b0 = *reinterpret_cast<const float4 *>(brow + tx * 4);
+                    const float4 b1 = *reinterpret_cast<const float4 *>(brow + 64 + tx * 4);
+                    const unsigned long long bp[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y),
+                                                      f2_pack(b1.z, b1.w)};
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const float av = reinterpret_cast<const float *>(&a[i])[kk];
+                        const unsigned long long ai = f2_pack(av, av);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) acc[i][j] = ffma2(ai, bp[j], acc[i][j]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) sgt::mbar_arrive(&empty[s]);  // this warp is done with the stage
+        }
+        if (!ok) break;
+        // epilogue: rows ty + 16 i, columns tx * 4 and 64 + tx * 4 (4 each)
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = m0 + ty + 16 * i;
+            if (r >= M) continue;
+#pragma unroll
+            for (int hb = 0; hb < 2; hb++) {
+                const int c = n0 + hb * 64 + tx * 4;
+                float4 o;
+                f2_unpack(acc[i][hb * 2], o.x, o.y);
+                f2_unpack(acc[i][hb * 2 + 1], o.z, o.w);
+                float *p = C + (size_t)r * N + c;
+                if (c + 3 < N) {
+                    *reinterpret_cast<float4 *>(p) = o;
+                } else {
+                    if (c + 0 < N) p[0] = o.x;
+                    if (c + 1 < N) p[1] = o.y;
+                    if (c + 2 < N) p[2] = o.z;
+                }
+            }
+        }
+    }
+}

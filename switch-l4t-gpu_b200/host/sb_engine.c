@@ -790,6 +790,12 @@ int sb_engine_profile(sb_engine *e, int which, int reps, void *flush, size_t flu
     return 0;
 }
 
+const char *sb_engine_step_kernel(sb_engine *e) {
+    if (!e) return "";
+    if (!e->mk) return e->model == SB_MODEL_QWEN ? "qwen per-stage kernels" : "gpt2 per-stage kernels";
+    return e->model == SB_MODEL_QWEN ? (e->mk2 ? "qwen_decode_mk2" : "qwen_decode_mk") : "gpt2_decode_mk";
+}
+
 int sb_engine_uses_persistent_kernel(sb_engine *e) { return e && e->mk; }
 
 int sb_engine_set_test_stall(sb_engine *e, int cta) {

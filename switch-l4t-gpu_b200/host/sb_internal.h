@@ -16,6 +16,12 @@ enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_TC, M_COUNT };
 typedef enum {
     F_SGEMM_B200 = 0,
     F_SGEMM_B200_SK,
+    F_SGEMM_TMA,
+    F_GEMM_HH_CC1,
+    F_GEMM_HH_CC2,
+    F_GEMM_HH_CC4,
+    F_GEMM_HH_CC8,
+    F_GEMM_HH_CC16,
     F_SGEMM_NAIVE,
     F_MEMBW,
     F_FMA_PEAK,

@@ -255,6 +255,24 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     if (N == 0) return 0;
+    /* Small batches on short outputs (fewer four-row tasks than two per SM):
+     * the tensor cores would split K and need a second launch; the split-K
+     * CUDA-core kernels keep fp16 subnormals as the tensor pipe does, with up
+     * to 16 activation rows per launch. */
+    if (B <= 16 && CEIL_DIV(N, 4) < 2L * c->sms) {
+        const long tasks = CEIL_DIV(N, 4);
+        for (int b0 = 0; b0 < B;) {
+            const int nb = B - b0 >= 16 ? 16 : B - b0 >= 8 ? 8 : B - b0 >= 4 ? 4 : B - b0 >= 2 ? 2 : 1;
+            const sb_fn_id f = nb == 16 ? F_GEMM_HH_CC16 : nb == 8 ? F_GEMM_HH_CC8 : nb == 4 ? F_GEMM_HH_CC4
+                                                                   : nb == 2 ? F_GEMM_HH_CC2 : F_GEMM_HH_CC1;
+            CUdeviceptr w = DP(W), xx = DP(X + (size_t)b0 * K), yy = DP(Y + (size_t)b0 * N);
+            void *args[] = {&w, &xx, &yy, &K, &N};
+            int rc = sb_launch(c, f, (unsigned)tasks, 1, 256, 0, (CUstream)stream, args, 0);
+            if (rc) return rc;
+            b0 += nb;
+        }
+        return 0;
+    }
     const int n_pad = CEIL_DIV(B, 16) * 16;
     CUtensorMap tw, tx;
     int rc = encode_kmajor_fp16(&tw, W, K, N, 128);
@@ -299,6 +317,40 @@ static int encode_kmajor_f32(CUtensorMap *tm, const void *base, int K, int rows)
                                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
     return 0;
+}
+
+/* B [K][N] fp32 row-major, box {128 n, 32 k}, dense (no swizzle) */
+static int encode_rowmajor_f32_b(CUtensorMap *tm, const void *base, int K, int N) {
+    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K}, strides[1] = {(cuuint64_t)N * 4};
+    const cuuint32_t box[2] = {128, 32}, estr[2] = {1, 1};
+    SB_CK(cuTensorMapEncodeTiled(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+    return 0;
+}
+
+int sb_sgemm_tma(const float *A, const float *B, float *C, int M, int N, int K, void *stream) {
+    SB_ARG(M >= 0 && N >= 0 && K >= 0, "bad SGEMM shape");
+    SB_ARG(A && B && C, "null pointer");
+    SB_ARG(K % 4 == 0 && N % 4 == 0 && ALIGNED16(A) && ALIGNED16(B) && ALIGNED16(C),
+           "sb_sgemm_tma needs K % 4 == 0, N % 4 == 0 and 16-byte aligned pointers");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (M == 0 || N == 0) return 0;
+    if (K == 0) {
+        for (int r = 0; r < M; r++) SB_CK(cuMemsetD32Async(DP(C + (size_t)r * N), 0, (size_t)N, (CUstream)stream));
+        return 0;
+    }
+    CUtensorMap ta, tb;
+    int rc = encode_kmajor_f32(&ta, A, K, M);
+    if (!rc) rc = encode_rowmajor_f32_b(&tb, B, K, N);
+    if (rc) return rc;
+    const long tiles = (long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128);
+    const unsigned grid = (unsigned)(tiles < c->sms ? tiles : c->sms);
+    const unsigned smem = 1024 + 4 * 32768 + 128;
+    CUdeviceptr cc = DP(C);
+    void *args[] = {&ta, &tb, &cc, &M, &N, &K};
+    return sb_launch(c, F_SGEMM_TMA, grid, 1, 288, smem, (CUstream)stream, args, 0);
 }
 
 /* C = A . Bt^T with A [M][K] and Bt [N][K] both K-major (the kernel's operand form). */
@@ -374,6 +426,18 @@ int sb_sgemm_nt_3xtf32(const float *A, const float *Bt, float *C, int M, int N, 
     if (M == 0 || N == 0) return 0;
     SB_ARG((long)CEIL_DIV(M, 128) * CEIL_DIV(N, 128) < 0x7fffffffL / 148, "sgemm_nt_3xtf32: too many tiles");
     return sgemm3x_launch(c, A, Bt, C, M, N, K, stream);
+}
+
+int sb_tc_set_test_skip(int chunk) {
+    SB_ARG(chunk >= -1, "chunk must be >= -1");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr p;
+    size_t bytes;
+    SB_CK(cuCtxSynchronize());
+    SB_CK(cuModuleGetGlobal(&p, &bytes, c->mod[M_TC], "tc_test_skip"));
+    SB_CK(cuMemsetD32(p, (unsigned)(chunk + 1), 1));
+    return 0;
 }
 
 int sb_tc_error(int *err) {

@@ -93,6 +93,8 @@ def lib():
     _sig(L.sb_attn_decode_noalloc, I, P, P, P, P, I, I, I, I, I, F, P)
     _sig(L.sb_layernorm, I, P, P, P, P, I, F, I, P)
     _sig(L.sb_gelu, I, P, P, I, P)
+    _sig(L.sb_tc_set_test_skip, I, I)
+    _sig(L.sb_sgemm_tma, I, P, P, P, I, I, I, P)
     _sig(L.sb_nccl_unique_id, I, P)
     _sig(L.sb_nccl_comm_init, I, P, I, P, I, ctypes.c_double)
     _sig(L.sb_nccl_comm_destroy, I, P, ctypes.c_double)
@@ -103,6 +105,7 @@ def lib():
     _sig(L.sb_engine_destroy, None, P)
     _sig(L.sb_engine_reset, I, P)
     _sig(L.sb_engine_kv_cache, I, P, P, P, P, P, P)
+    _sig(L.sb_engine_step_kernel, ctypes.c_char_p, P)
     _sig(L.sb_engine_forward, I, P, I, I, I, P)
     _sig(L.sb_engine_generate, I, P, P, I, I, P, ctypes.POINTER(I), ctypes.c_uint)
     _sig(L.sb_engine_begin, I, P, P, I, I, ctypes.c_uint)
@@ -170,6 +173,11 @@ def module_image(name):
 
 def sgemm(A, B, C, M, N, K, stream=None):
     check(lib().sb_sgemm(_p(A), _p(B), _p(C), M, N, K, _s(stream)))
+
+
+def sgemm_tma(A, B, C, M, N, K, stream=None):
+    """The TMA-staged CUDA-core SGEMM (bit-identical to sgemm)."""
+    check(lib().sb_sgemm_tma(_p(A), _p(B), _p(C), M, N, K, _s(stream)))
 
 
 def sgemm_rows(A, B, C, M, N, K, row0, row1, stream=None):
@@ -349,6 +357,11 @@ class Engine:
         """Failure-detection test hook: CTA `cta` withholds its layer-0
         outputs (-1: off); see sb_engine_set_test_stall."""
         check(lib().sb_engine_set_test_stall(self.h, cta))
+
+    @property
+    def step_kernel(self):
+        """Name of the kernel that runs the decode step."""
+        return lib().sb_engine_step_kernel(self.h).decode()
 
     @property
     def persistent(self):

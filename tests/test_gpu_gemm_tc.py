@@ -69,3 +69,72 @@ def test_gemm_hh_rejects_bad_shapes(cuda_dev):
         sb200.gemm_hh(W, X, Y, 12, 64, 2)  # K % 8 != 0
     with pytest.raises(sb200.SbError):
         sb200.gemm_hh(W, X, Y, 8, 64, 257)  # batch > 256
+
+
+@pytest.mark.parametrize("N,K,B,skip", [(1024, 1024, 32, 0), (4096, 2048, 16, 5)])
+def test_gemm_hh_wait_timeout_recovers(cuda_dev, N, K, B, skip):
+    """Failure detection on the tensor-core kernel without a GPU fault: the
+    test hook makes every TMA producer stop before K-chunk `skip`, so the
+    MMA issuer's bounded wait for that stage runs out (~2 s).  The kernel
+    drains the copies it issued, frees its tensor memory and returns;
+    sb_tc_error reports the timeout; with the hook off the next call on the
+    same context matches the oracle again."""
+    import time
+
+    import torch
+    W = _flushed_h(N * K, 0.02, 5 + N).reshape(N, K)
+    X = _flushed_h(B * K, 1.0, 6 + K).reshape(B, K)
+    dW = torch.from_numpy(W.view(np.int16)).cuda()
+    dX = torch.from_numpy(X.view(np.int16)).cuda()
+    dY = torch.zeros((B, N), device="cuda")
+    assert sb200.tc_error() == 0
+    sb200.check(sb200.lib().sb_tc_set_test_skip(skip))
+    try:
+        t0 = time.time()
+        sb200.gemm_hh(dW, dX, dY, K, N, B)
+        torch.cuda.synchronize()
+        assert sb200.tc_error() != 0
+        assert time.time() - t0 < 30
+    finally:
+        sb200.check(sb200.lib().sb_tc_set_test_skip(-1))
+    dY.fill_(float("nan"))
+    sb200.gemm_hh(dW, dX, dY, K, N, B)
+    torch.cuda.synchronize()
+    assert sb200.tc_error() == 0
+    Y = dY.cpu().numpy()
+    for b in (0, B - 1):
+        want = orc.gemv_h(W, orc.h2f(X[b]))
+        rel = np.linalg.norm((Y[b] - want).astype(np.float64)) / np.linalg.norm(want.astype(np.float64))
+        assert rel <= TOL
+
+
+@pytest.mark.parametrize("N,K,B", [(896, 896, 4), (896, 4864, 16), (896, 896, 13), (640, 512, 24)])
+def test_gemm_hh_keeps_subnormals(cuda_dev, N, K, B):
+    """sb_gemm_hh uses fp16 subnormals as subnormals on both of its paths:
+    small batches on short outputs (the CUDA-core form) and the tensor cores
+    (B = 24).  Activation rows like the prefill's lo rows (x - fp16(x)), half
+    of them subnormal, against an FP64 product of the IEEE decodes; and the
+    result differs from what a flush to zero would give."""
+    import torch
+    rng = np.random.default_rng(N + K + B)
+    W = _flushed_h(N * K, 0.02, 3 + N).reshape(N, K)
+    xs = rng.normal(0, 1, (B, K)).astype(np.float32)
+    hi = xs.astype(np.float16)
+    lo = (xs - hi.astype(np.float32)).astype(np.float16)
+    lo[:, ::2] = (lo[:, ::2].astype(np.float32) * 2.0 ** -8).astype(np.float16)  # more subnormals
+    bits = lo.view(np.uint16)
+    assert (((bits & 0x7C00) == 0) & ((bits & 0x3FF) != 0)).mean() > 0.3
+    dW = torch.from_numpy(W.view(np.int16)).cuda()
+    dX = torch.from_numpy(lo.view(np.int16).copy()).cuda()
+    dY = torch.full((B, N), float("nan"), device="cuda")
+    sb200.gemm_hh(dW, dX, dY, K, N, B)
+    torch.cuda.synchronize()
+    assert sb200.tc_error() == 0
+    Y = dY.cpu().numpy().astype(np.float64)
+    want = lo.astype(np.float64) @ W.view(np.float16).astype(np.float64).T
+    rel = np.linalg.norm(Y - want) / np.linalg.norm(want)
+    assert rel <= 1e-5, rel
+    flushed = lo.copy()
+    flushed[(flushed.view(np.uint16) & 0x7C00) == 0] = 0
+    want_ftz = flushed.astype(np.float64) @ W.view(np.float16).astype(np.float64).T
+    assert np.linalg.norm(Y - want_ftz) / np.linalg.norm(want_ftz) > 10 * rel
