@@ -588,7 +588,7 @@ def gemv_section(torch, dev):
                                      "launches": "CUDA-graph replay of %d" % reps}
     del pool
     torch.cuda.empty_cache()
-    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1, or gemv_hh_sk1 (split-K) below 2 x SMs four-row tasks (CUDA cores); b4, b16: gemm_hh_tc (tcgen05)",
+    return {"metric": "FP16 GEMV HBM GB/s", "kernel": "b1: gemv_hh1, or gemv_hh_sk1 (split-K) below 2 x SMs four-row tasks (CUDA cores); b4, b16: gemm_hh_tc (tcgen05), or gemm_hh_mma8/16 (mma.sync, one launch) below 2 x SMs eight-row tiles",
             "peak": peak, "unit": "GB/s", "shapes": out}
 
 

@@ -137,9 +137,10 @@ int sb_gemv_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
  * tensor pipe does not flush them).  K % 8 == 0; W, X 16-byte aligned.
  * Short matrices are split along K through a library-owned workspace and
  * summed in split order, so results are deterministic; batches of up to 16
- * rows on short outputs (fewer than 8 rows per SM) run on the CUDA cores
- * instead (the mixed-precision FMA, subnormals kept likewise, one launch per
- * 16 rows).  No counterpart in the reference (its prefill is gemv_multi,
+ * rows on short outputs (fewer than 16 rows per SM) run in one launch on
+ * mma.sync tiles instead (fp16 in, FP32 accumulation, subnormals kept
+ * likewise; K split over a CTA's warps, partials added in warp order).  No
+ * counterpart in the reference (its prefill is gemv_multi,
  * gpt2_kernels.cu:115-155). */
 int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int B, void *stream);
 /* Opt-in SGEMM on the TF32 tensor pipe with the 3xTF32 split (big/small

@@ -235,13 +235,10 @@ extern "C" __global__ void __launch_bounds__(256) gemv_hh4(const unsigned short 
 // global memory (L1-cached, shared by the CTAs of an SM) and flushed per
 // use, so there is no staging round trip.  Warp partials are added in
 // warp order in shared memory.  Block 256.
-// KEEP: fp16 subnormals of W and X used as subnormals (the tensor pipe's
-// semantics, for sb_gemm_hh's small batches) instead of the reference's
-// flush to zero.  Fewer k-chunks in flight for wide batches (registers).
-template <int B, bool KEEP = false>
+template <int B>
 __device__ void gemv_hh_sk_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
                                 float *__restrict__ Y, int K, int N) {
-    constexpr int R = 4, NW = 8, U = B <= 4 ? 4 : (B <= 8 ? 2 : 1);
+    constexpr int R = 4, NW = 8, U = 4;
     __shared__ float part[NW][R * B];
     const int cpr = K / 8, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int per = (cpr + NW - 1) / NW;
@@ -273,15 +270,10 @@ __device__ void gemv_hh_sk_body(const unsigned short *__restrict__ W, const unsi
 #pragma unroll
                     for (int b = 0; b < B; b++) {
                         const uint4 v = __ldg(X4 + (long)b * cpr + c);
-                        if (KEEP) {
+                        const uint4 x = make_uint4(ftz_half2_bits(v.x), ftz_half2_bits(v.y), ftz_half2_bits(v.z),
+                                                   ftz_half2_bits(v.w));
 #pragma unroll
-                            for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh_keep(w[u][r], v, acc[r][b]);
-                        } else {
-                            const uint4 x = make_uint4(ftz_half2_bits(v.x), ftz_half2_bits(v.y), ftz_half2_bits(v.z),
-                                                       ftz_half2_bits(v.w));
-#pragma unroll
-                            for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh(w[u][r], x, acc[r][b]);
-                        }
+                        for (int r = 0; r < R; r++) acc[r][b] = dot_chunk_hh(w[u][r], x, acc[r][b]);
                     }
                 }
             }
@@ -317,29 +309,82 @@ extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk4(const unsigned sho
     gemv_hh_sk_body<4>(W, X, Y, K, N);
 }
 
-// sb_gemm_hh's small batches (B <= 16) on short outputs, where the tensor
-// cores would split K and add a second launch: the split-K CUDA-core form
-// with subnormals kept (the tensor pipe's semantics), B activation rows per
-// launch.
-extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc1(const unsigned short *W, const unsigned short *X,
-                                                              float *Y, int K, int N) {
-    gemv_hh_sk_body<1, true>(W, X, Y, K, N);
+// sb_gemm_hh's small batches (B <= 16) on short outputs (fewer than ~300
+// row tiles), in ONE launch: the tcgen05 kernel needs split-K there, with a
+// second launch to add the partials, and the CUDA-core dot needs B fma per
+// weight.  One CTA per 8 rows of W; its 16 warps take contiguous sixteenths
+// of K and add their partial tiles in warp order in shared memory
+// (deterministic).  The products run on mma.sync m16n8k16 (fp16 in, FP32
+// accumulation; fp16 subnormals kept, as the tensor pipe of gemm_hh_tc):
+// A = 16 activation rows (zero beyond B), B = 8 weight rows (zero beyond N).
+// Per 32-element K block, lane (g, q) holds elements 8q .. 8q+7 of its
+// rows: the first four in the block's first MMA's fragment slots, the last
+// four in the second's -- the same order for both operands, so every
+// weight still meets its own activation -- and loads them as one 16-byte
+// chunk (W streamed past L1, X through L1).  A warp issues the loads of up
+// to U blocks before their MMAs: a CTA keeps its whole slice of W in flight
+// for K up to 16 x U x 32.  WIDE: B > 8 (rows g + 8 of A).
+// grid ceil(N/8); block 512.  K % 8 == 0.
+template <bool WIDE>
+__device__ void gemm_hh_mma_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
+                                 float *__restrict__ Y, int K, int N, int B) {
+    constexpr int NW = 16, U = WIDE ? 8 : 10;
+    __shared__ float red[NW][32][4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    const int n0 = blockIdx.x * 8, nblk = (K + 31) / 32;
+    const int blk0 = nblk * warp / NW, blk1 = nblk * (warp + 1) / NW;
+    const bool wrow = n0 + g < N, xr0 = g < B, xr1 = WIDE && g + 8 < B;
+    const uint4 *wp = reinterpret_cast<const uint4 *>(W + (long)(n0 + g) * K) + q;
+    const uint4 *x0p = reinterpret_cast<const uint4 *>(X + (long)g * K) + q;
+    const uint4 *x1p = reinterpret_cast<const uint4 *>(X + (long)(g + 8) * K) + q;
+    const int kc = K / 8;  // 16-byte chunks per row
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = blk0; b < blk1; b += U) {
+        uint4 w[U], a[U], c[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int ch = (b + u) * 4;  // this lane's chunk: ch + q
+            const bool ok = b + u < blk1 && ch + q < kc;
+            w[u] = ok && wrow ? ld_stream_u4(wp + ch) : make_uint4(0u, 0u, 0u, 0u);
+            a[u] = ok && xr0 ? __ldg(x0p + ch) : make_uint4(0u, 0u, 0u, 0u);
+            c[u] = ok && xr1 ? __ldg(x1p + ch) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (b + u >= blk1) break;
+            float(&d)[4] = (u & 1) ? d1 : d0;
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                "{%0, %1, %2, %3};"
+                : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                : "r"(a[u].x), "r"(c[u].x), "r"(a[u].y), "r"(c[u].y), "r"(w[u].x), "r"(w[u].y));
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                "{%0, %1, %2, %3};"
+                : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                : "r"(a[u].z), "r"(c[u].z), "r"(a[u].w), "r"(c[u].w), "r"(w[u].z), "r"(w[u].w));
+        }
+    }
+    // D[b][n]: lane (g, q) holds (b = g, n = 2q, 2q+1) and (b = g + 8, same n)
+#pragma unroll
+    for (int i = 0; i < 4; i++) red[warp][lane][i] = d0[i] + d1[i];
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int l = threadIdx.x >> 2, i = threadIdx.x & 3;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) s += red[w][l][i];
+        const int b = (l >> 2) + ((i >> 1) << 3), n = n0 + 2 * (l & 3) + (i & 1);
+        if (b < B && n < N) Y[(long)b * N + n] = s;
+    }
 }
-extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc2(const unsigned short *W, const unsigned short *X,
-                                                              float *Y, int K, int N) {
-    gemv_hh_sk_body<2, true>(W, X, Y, K, N);
+extern "C" __global__ void __launch_bounds__(512) gemm_hh_mma8(const unsigned short *W, const unsigned short *X,
+                                                               float *Y, int K, int N, int B) {
+    gemm_hh_mma_body<false>(W, X, Y, K, N, B);
 }
-extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc4(const unsigned short *W, const unsigned short *X,
-                                                              float *Y, int K, int N) {
-    gemv_hh_sk_body<4, true>(W, X, Y, K, N);
-}
-extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc8(const unsigned short *W, const unsigned short *X,
-                                                              float *Y, int K, int N) {
-    gemv_hh_sk_body<8, true>(W, X, Y, K, N);
-}
-extern "C" __global__ void __launch_bounds__(256) gemm_hh_cc16(const unsigned short *W, const unsigned short *X,
-                                                               float *Y, int K, int N) {
-    gemv_hh_sk_body<16, true>(W, X, Y, K, N);
+extern "C" __global__ void __launch_bounds__(512) gemm_hh_mma16(const unsigned short *W, const unsigned short *X,
+                                                                float *Y, int K, int N, int B) {
+    gemm_hh_mma_body<true>(W, X, Y, K, N, B);
 }
 
 // GQA decode attention with an explicit T (no step state); 7 query heads

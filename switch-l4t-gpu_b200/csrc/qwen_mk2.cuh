@@ -334,7 +334,6 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
         qmk::rms_regs(xv, gw1, xhw, xlw, red, eps);
         __syncthreads();
         xstamp(l, 0);  // S1 norm done
-        if (prefetcher) prefetch_piece(l + 1, 0);
         wait_slot(MB_HEAD);
         __syncwarp();
         xstamp(l, 1);  // S1 rows landed
@@ -367,6 +366,9 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             else if (h >= NH) kc[(long)pos * KVD + r - C] = y;
         }
         stamp(l, 0, 1);
+        // (issued here rather than before the S1 dot: the prefetch instructions
+        // of one warp delayed the CTA's S1 barrier, 6 us per token)
+        if (prefetcher) prefetch_piece(l + 1, 0);
         // gate/up rows (head slot: S1's rows are consumed) and this layer's
         // W_downT rows stream in while attention runs; a CTA with an
         // attention item issues them after it
@@ -636,6 +638,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             }
         }
         stamp(l, 3, 1);
+        if (l + 1 < NL) s1_consts(l + 1);  // the loads' latency hides in the S5 wait
         // ================= S5: this CTA's residual rows += the down partials
         // of all CTAs (summed in CTA order) -> x words
         if (prefetcher) prefetch_piece(l + 1, 4);
@@ -680,8 +683,6 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             fence_async();
             copy_s1(l + 1);
             xstamp(l, 7);  // S5 next S1 rows issued
-            s1_consts(l + 1);
-            xstamp(l, 8);  // S5 next S1 constants loaded
         }
     }
     if (aborted) {

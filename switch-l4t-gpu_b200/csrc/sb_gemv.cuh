@@ -83,17 +83,6 @@ SB_DEV float dot_chunk_hh(const uint4 &w, const uint4 &x, float acc) {
     }
     return acc;
 }
-// The same dot with fp16 subnormals used as subnormals (no flush of either
-// operand): the semantics of the tensor pipe (sb_gemm_hh).
-SB_DEV float dot_chunk_hh_keep(const uint4 &w, const uint4 &x, float acc) {
-    const unsigned ws[4] = {w.x, w.y, w.z, w.w}, xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        acc = fma_hh(acc, (unsigned short)(ws[j] & 0xffffu), (unsigned short)(xs[j] & 0xffffu));
-        acc = fma_hh(acc, (unsigned short)(ws[j] >> 16), (unsigned short)(xs[j] >> 16));
-    }
-    return acc;
-}
 SB_DEV float dot_chunk(WF, const uint4 &w, const float4 &a, float acc) {
     acc = fmaf(__uint_as_float(w.x), a.x, acc);
     acc = fmaf(__uint_as_float(w.y), a.y, acc);

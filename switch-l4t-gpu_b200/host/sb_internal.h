@@ -17,11 +17,8 @@ typedef enum {
     F_SGEMM_B200 = 0,
     F_SGEMM_B200_SK,
     F_SGEMM_TMA,
-    F_GEMM_HH_CC1,
-    F_GEMM_HH_CC2,
-    F_GEMM_HH_CC4,
-    F_GEMM_HH_CC8,
-    F_GEMM_HH_CC16,
+    F_GEMM_HH_MMA8,
+    F_GEMM_HH_MMA16,
     F_SGEMM_NAIVE,
     F_MEMBW,
     F_FMA_PEAK,

@@ -255,23 +255,15 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     if (N == 0) return 0;
-    /* Small batches on short outputs (fewer four-row tasks than two per SM):
-     * the tensor cores would split K and need a second launch; the split-K
-     * CUDA-core kernels keep fp16 subnormals as the tensor pipe does, with up
-     * to 16 activation rows per launch. */
-    if (B <= 16 && CEIL_DIV(N, 4) < 2L * c->sms) {
-        const long tasks = CEIL_DIV(N, 4);
-        for (int b0 = 0; b0 < B;) {
-            const int nb = B - b0 >= 16 ? 16 : B - b0 >= 8 ? 8 : B - b0 >= 4 ? 4 : B - b0 >= 2 ? 2 : 1;
-            const sb_fn_id f = nb == 16 ? F_GEMM_HH_CC16 : nb == 8 ? F_GEMM_HH_CC8 : nb == 4 ? F_GEMM_HH_CC4
-                                                                   : nb == 2 ? F_GEMM_HH_CC2 : F_GEMM_HH_CC1;
-            CUdeviceptr w = DP(W), xx = DP(X + (size_t)b0 * K), yy = DP(Y + (size_t)b0 * N);
-            void *args[] = {&w, &xx, &yy, &K, &N};
-            int rc = sb_launch(c, f, (unsigned)tasks, 1, 256, 0, (CUstream)stream, args, 0);
-            if (rc) return rc;
-            b0 += nb;
-        }
-        return 0;
+    /* Small batches on short outputs (fewer 8-row tiles than ~2 per SM): the
+     * tcgen05 kernel would split K and need a second launch; gemm_hh_mma*
+     * (mma.sync, same fp16-in / FP32-accumulate semantics, subnormals kept)
+     * does it in one launch, one CTA per 8 rows of W. */
+    if (B <= 16 && CEIL_DIV(N, 8) < 2L * c->sms) {
+        const sb_fn_id f = B > 8 ? F_GEMM_HH_MMA16 : F_GEMM_HH_MMA8;
+        CUdeviceptr w = DP(W), xx = DP(X), yy = DP(Y);
+        void *args[] = {&w, &xx, &yy, &K, &N, &B};
+        return sb_launch(c, f, (unsigned)CEIL_DIV(N, 8), 1, 512, 0, (CUstream)stream, args, 0);
     }
     const int n_pad = CEIL_DIV(B, 16) * 16;
     CUtensorMap tw, tx;

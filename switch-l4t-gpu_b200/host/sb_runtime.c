@@ -36,11 +36,8 @@ static const struct {
     [F_SGEMM_B200] = {M_SWITCH, "sgemm_b200"},
     [F_SGEMM_B200_SK] = {M_SWITCH, "sgemm_b200_sk"},
     [F_SGEMM_TMA] = {M_TC, "sgemm_tma"},
-    [F_GEMM_HH_CC1] = {M_QWEN, "gemm_hh_cc1"},
-    [F_GEMM_HH_CC2] = {M_QWEN, "gemm_hh_cc2"},
-    [F_GEMM_HH_CC4] = {M_QWEN, "gemm_hh_cc4"},
-    [F_GEMM_HH_CC8] = {M_QWEN, "gemm_hh_cc8"},
-    [F_GEMM_HH_CC16] = {M_QWEN, "gemm_hh_cc16"},
+    [F_GEMM_HH_MMA8] = {M_QWEN, "gemm_hh_mma8"},
+    [F_GEMM_HH_MMA16] = {M_QWEN, "gemm_hh_mma16"},
     [F_SGEMM_NAIVE] = {M_SWITCH, "sgemm_naive"},
     [F_MEMBW] = {M_SWITCH, "membw_read4"},
     [F_FMA_PEAK] = {M_SWITCH, "fma_peak"},
