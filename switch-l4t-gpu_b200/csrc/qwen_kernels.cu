@@ -323,12 +323,13 @@ extern "C" __global__ void __launch_bounds__(256) gemv_hh_sk4(const unsigned sho
 // weight still meets its own activation -- and loads them as one 16-byte
 // chunk (W streamed past L1, X through L1).  A warp issues the loads of up
 // to U blocks before their MMAs: a CTA keeps its whole slice of W in flight
-// for K up to 16 x U x 32.  WIDE: B > 8 (rows g + 8 of A).
-// grid ceil(N/8); block 512.  K % 8 == 0.
-template <bool WIDE>
+// for K up to NW x U x 32.  WIDE: B > 8 (rows g + 8 of A).  NW = 16 for
+// fewer tiles than SMs can hold twice; NW = 4 (four CTAs per SM) for more.
+// grid ceil(N/8); block 32 NW.  K % 8 == 0.
+template <bool WIDE, int NW>
 __device__ void gemm_hh_mma_body(const unsigned short *__restrict__ W, const unsigned short *__restrict__ X,
                                  float *__restrict__ Y, int K, int N, int B) {
-    constexpr int NW = 16, U = WIDE ? 8 : 10;
+    constexpr int U = WIDE ? 8 : 10;
     __shared__ float red[NW][32][4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
     const int n0 = blockIdx.x * 8, nblk = (K + 31) / 32;
@@ -380,11 +381,19 @@ __device__ void gemm_hh_mma_body(const unsigned short *__restrict__ W, const uns
 }
 extern "C" __global__ void __launch_bounds__(512) gemm_hh_mma8(const unsigned short *W, const unsigned short *X,
                                                                float *Y, int K, int N, int B) {
-    gemm_hh_mma_body<false>(W, X, Y, K, N, B);
+    gemm_hh_mma_body<false, 16>(W, X, Y, K, N, B);
 }
 extern "C" __global__ void __launch_bounds__(512) gemm_hh_mma16(const unsigned short *W, const unsigned short *X,
                                                                 float *Y, int K, int N, int B) {
-    gemm_hh_mma_body<true>(W, X, Y, K, N, B);
+    gemm_hh_mma_body<true, 16>(W, X, Y, K, N, B);
+}
+extern "C" __global__ void __launch_bounds__(128, 4)
+    gemm_hh_mma8_w4(const unsigned short *W, const unsigned short *X, float *Y, int K, int N, int B) {
+    gemm_hh_mma_body<false, 4>(W, X, Y, K, N, B);
+}
+extern "C" __global__ void __launch_bounds__(128, 4)
+    gemm_hh_mma16_w4(const unsigned short *W, const unsigned short *X, float *Y, int K, int N, int B) {
+    gemm_hh_mma_body<true, 4>(W, X, Y, K, N, B);
 }
 
 // GQA decode attention with an explicit T (no step state); 7 query heads

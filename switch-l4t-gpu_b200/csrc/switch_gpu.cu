@@ -76,7 +76,9 @@ __device__ __forceinline__ void sg_store_slice(SgSmem &s, int buf, int ams, int 
 
 // k range [kbeg, kbeg + klen) of the product (split-K: the unpredicated
 // path only, kbeg and klen multiples of SG_BK); K stays A's row stride.
-template <bool EDGE>
+// LOCAL: the tile is written to C as a compact 128 x 128 block (a piece of
+// a tile in the stream-K form) instead of at its place in the M x N matrix.
+template <bool EDGE, bool LOCAL = false>
 __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const float *__restrict__ B,
                                             float *__restrict__ C, int M, int N, int K, int tid, int cta,
                                             int ncta, SgSmem &s, int kbeg = 0, int klen = -1) {
@@ -171,7 +173,7 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
                 float4 o;
                 f2_unpack(acc[i][hb * 2], o.x, o.y);
                 f2_unpack(acc[i][hb * 2 + 1], o.z, o.w);
-                float *p = C + (size_t)r * N + c;
+                float *p = LOCAL ? C + (size_t)(r - m0) * SG_BN + (c - n0) : C + (size_t)r * N + c;
                 if (!EDGE) {
                     *reinterpret_cast<float4 *>(p) = o;
                 } else if (r < M) {
@@ -259,6 +261,63 @@ extern "C" __global__ void __launch_bounds__(256, 2)
     if (tile >= tiles) return;
     const int klen = K / splits;
     sgemm_tiles<false>(A, B, ws + (size_t)split * M * N, M, N, K, threadIdx.x, tile, tiles, s, split * klen, klen);
+}
+
+// Stream-K form for products with fewer 128 x 128 tiles than two per SM
+// (1024^3: 64 tiles): the tiles x K/16 k-chunks of the product are cut into
+// gridDim.x equal contiguous ranges, one per CTA (two per SM), so every SM
+// gets the same work -- split-K over 4 left 40 of 148 SMs with one CTA
+// and the rest with two.  A range covers at most two tiles (it is shorter
+// than one tile's K); each piece goes to ws[2 * cta + piece] (a compact
+// 128 x 128 tile), and sgemm_stk_fixup adds a tile's pieces in CTA order
+// (deterministic) into C.
+// Needs M, N % 128 == 0, K % 16 == 0, tiles < gridDim.x and 16-byte aligned
+// pointers (the host checks).  Block 256.
+__device__ __forceinline__ long stk_first(long units, int g, int c) { return units * c / g; }
+// the CTA whose range holds unit u: the largest c with units * c / g <= u
+__device__ __forceinline__ int stk_owner(long units, int g, long u) { return (int)(((u + 1) * g - 1) / units); }
+extern "C" __global__ void __launch_bounds__(256, 2)
+    sgemm_b200_stk(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C,
+                   float *__restrict__ ws, int M, int N, int K) {
+    if (blockDim.x * blockDim.y * blockDim.z != SG_THREADS) return;
+    __shared__ __align__(16) SgSmem s;
+    const int tiles = (M / SG_BM) * (N / SG_BN), nk = K / SG_BK, G = gridDim.x, cta = blockIdx.x;
+    const long units = (long)tiles * nk, u1 = stk_first(units, G, cta + 1);
+    int piece = 0;
+    for (long u = stk_first(units, G, cta); u < u1; piece++) {
+        const int t = (int)(u / nk), k0 = (int)(u % nk);
+        const int k1 = (int)min((long)nk, u1 - (long)t * nk);
+        sgemm_tiles<false, true>(A, B, ws + (size_t)(2 * cta + piece) * SG_BM * SG_BN, M, N, K, threadIdx.x, t,
+                                 tiles, s, k0 * SG_BK, (k1 - k0) * SG_BK);
+        u = (long)t * nk + k1;
+    }
+}
+// C tile t = the sum, in CTA order, of its pieces in ws.  grid: tiles x 4
+// (a quarter of a tile per CTA); block 256; G = sgemm_b200_stk's grid.
+extern "C" __global__ void sgemm_stk_fixup(const float *__restrict__ ws, float *__restrict__ C, int M, int N, int K,
+                                           int G) {
+    const int tiles_n = N / SG_BN, tiles = (M / SG_BM) * tiles_n, nk = K / SG_BK;
+    const int t = blockIdx.x / 4, quarter = blockIdx.x % 4;
+    if (t >= tiles) return;
+    const long units = (long)tiles * nk, ub = (long)t * nk, ue = ub + nk;
+    const int c_lo = stk_owner(units, G, ub), c_hi = stk_owner(units, G, ue - 1);
+    // the tile's row / column in sgemm_tiles' grouped raster
+    const int tiles_m = M / SG_BM, per_group = 8 * tiles_n, first_m = (t / per_group) * 8;
+    const int gsz = min(tiles_m - first_m, 8);
+    const int m0 = (first_m + (t % per_group) % gsz) * SG_BM, n0 = ((t % per_group) / gsz) * SG_BN;
+    for (int i = quarter * 1024 + threadIdx.x; i < (quarter + 1) * 1024; i += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = c_lo; c <= c_hi; c++) {
+            const int piece = (stk_first(units, G, c) / nk == t) ? 0 : 1;
+            const float4 v = reinterpret_cast<const float4 *>(ws + (size_t)(2 * c + piece) * SG_BM * SG_BN)[i];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const int r = (i * 4) / SG_BN, col = (i * 4) % SG_BN;
+        *reinterpret_cast<float4 *>(C + (size_t)(m0 + r) * N + n0 + col) = acc;
+    }
 }
 
 // One output per thread, k in order, product and sum rounded separately:

@@ -25,16 +25,6 @@ static int ws_reserve(sb_ctx *c, size_t need, CUdeviceptr *ws) {
 }
 
 /* ------------------------------------------------------------------ SGEMM */
-/* Split-K count for a product of `tiles` 128x128 tiles: enough CTAs to fill
- * two per SM, each still running at least 8 k-slices of 16; 1 = no split. */
-static int sgemm_splits(const sb_ctx *c, long tiles, int M, int N, int K, const void *A, const void *B,
-                        const void *C) {
-    if (M % 128 || N % 128 || !ALIGNED16(A) || !ALIGNED16(B) || !ALIGNED16(C)) return 1;
-    int s = (int)((2L * c->sms) / (tiles > 0 ? tiles : 1));
-    while (s > 1 && (K % (16 * s) || K / s < 128)) s--;
-    return s < 1 ? 1 : s;
-}
-
 int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
                   void *stream) {
     SB_ARG(M >= 0 && N >= 0 && K >= 0 && 0 <= row0 && row0 <= row1 && row1 <= M, "bad SGEMM shape");
@@ -47,22 +37,20 @@ int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K,
     /* one CTA per 128x128 tile (two resident per SM); the kernel's tile loop
      * covers the rest if the count ever exceeds the grid limit */
     const long tiles = (long)CEIL_DIV(m, 128) * CEIL_DIV(N, 128);
-    const int splits = tiles < c->sms ? sgemm_splits(c, tiles, m, N, K, (const void *)(uintptr_t)a, B,
-                                                     (const void *)(uintptr_t)cc)
-                                      : 1;
-    if (splits > 1) { /* small products: k split over CTAs, partial tiles added in split order */
+    if (tiles < 2L * c->sms && m % 128 == 0 && N % 128 == 0 && K % 16 == 0 && K > 0 && ALIGNED16(A) &&
+        ALIGNED16(B) && ALIGNED16(C + (size_t)row0 * N) && ALIGNED16(A + (size_t)row0 * K)) {
+        /* small products: stream-K -- the tiles' k-chunks cut into equal
+         * ranges, two CTAs per SM; partial tiles added in CTA order */
+        const long units = tiles * (K / 16);
+        int G = (int)(units < 2L * c->sms ? units : 2L * c->sms);
         CUdeviceptr ws;
-        int rc = ws_reserve(c, (size_t)splits * m * N * 4, &ws);
+        int rc = ws_reserve(c, (size_t)2 * G * 128 * 128 * 4, &ws);
         if (rc) return rc;
-        void *args[] = {&a, &b, &ws, (void *)&m, &N, &K, (void *)&splits};
-        rc = sb_launch(c, F_SGEMM_B200_SK, (unsigned)(tiles * splits), 1, 256, 0, (CUstream)stream, args, 0);
+        void *args[] = {&a, &b, &cc, &ws, (void *)&m, &N, &K};
+        rc = sb_launch(c, F_SGEMM_B200_STK, (unsigned)G, 1, 256, 0, (CUstream)stream, args, 0);
         if (rc) return rc;
-        long total = (long)m * N;
-        int sp = splits;
-        void *rargs[] = {&ws, &cc, &total, &sp};
-        long g = CEIL_DIV(total, 256 * 4);
-        if (g > 8L * c->sms) g = 8L * c->sms;
-        return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
+        void *fargs[] = {&ws, &cc, (void *)&m, &N, &K, &G};
+        return sb_launch(c, F_SGEMM_STK_FIXUP, (unsigned)(tiles * 4), 1, 256, 0, (CUstream)stream, fargs, 0);
     }
     const long grid = tiles < 0x7fffffffL ? tiles : 0x7fffffffL;
     void *args[] = {&a, &b, &cc, (void *)&m, &N, &K};
@@ -255,15 +243,19 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     if (N == 0) return 0;
-    /* Small batches on short outputs (fewer 8-row tiles than ~2 per SM): the
-     * tcgen05 kernel would split K and need a second launch; gemm_hh_mma*
-     * (mma.sync, same fp16-in / FP32-accumulate semantics, subnormals kept)
-     * does it in one launch, one CTA per 8 rows of W. */
-    if (B <= 16 && CEIL_DIV(N, 8) < 2L * c->sms) {
-        const sb_fn_id f = B > 8 ? F_GEMM_HH_MMA16 : F_GEMM_HH_MMA8;
+    /* Small batches on outputs shorter than 128 rows per SM: the tcgen05
+     * kernel would split K and need a second launch; gemm_hh_mma* (mma.sync,
+     * same fp16-in / FP32-accumulate semantics, subnormals kept) does it in
+     * one launch, one CTA per 8 rows of W. */
+    if (B <= 16 && N < 128L * c->sms) {
+        /* 16 warps per CTA while the tiles are fewer than two per SM, else 4
+         * (four CTAs per SM) */
+        const int wide = CEIL_DIV(N, 8) < 2L * c->sms;
+        const sb_fn_id f = wide ? (B > 8 ? F_GEMM_HH_MMA16 : F_GEMM_HH_MMA8)
+                                : (B > 8 ? F_GEMM_HH_MMA16_W4 : F_GEMM_HH_MMA8_W4);
         CUdeviceptr w = DP(W), xx = DP(X), yy = DP(Y);
         void *args[] = {&w, &xx, &yy, &K, &N, &B};
-        return sb_launch(c, f, (unsigned)CEIL_DIV(N, 8), 1, 512, 0, (CUstream)stream, args, 0);
+        return sb_launch(c, f, (unsigned)CEIL_DIV(N, 8), 1, wide ? 512 : 128, 0, (CUstream)stream, args, 0);
     }
     const int n_pad = CEIL_DIV(B, 16) * 16;
     CUtensorMap tw, tx;

@@ -35,9 +35,13 @@ static const struct {
 } fn_table[F_COUNT] = {
     [F_SGEMM_B200] = {M_SWITCH, "sgemm_b200"},
     [F_SGEMM_B200_SK] = {M_SWITCH, "sgemm_b200_sk"},
+    [F_SGEMM_B200_STK] = {M_SWITCH, "sgemm_b200_stk"},
+    [F_SGEMM_STK_FIXUP] = {M_SWITCH, "sgemm_stk_fixup"},
     [F_SGEMM_TMA] = {M_TC, "sgemm_tma"},
     [F_GEMM_HH_MMA8] = {M_QWEN, "gemm_hh_mma8"},
     [F_GEMM_HH_MMA16] = {M_QWEN, "gemm_hh_mma16"},
+    [F_GEMM_HH_MMA8_W4] = {M_QWEN, "gemm_hh_mma8_w4"},
+    [F_GEMM_HH_MMA16_W4] = {M_QWEN, "gemm_hh_mma16_w4"},
     [F_SGEMM_NAIVE] = {M_SWITCH, "sgemm_naive"},
     [F_MEMBW] = {M_SWITCH, "membw_read4"},
     [F_FMA_PEAK] = {M_SWITCH, "fma_peak"},

@@ -71,7 +71,9 @@ def test_gemm_hh_rejects_bad_shapes(cuda_dev):
         sb200.gemm_hh(W, X, Y, 8, 64, 257)  # batch > 256
 
 
-@pytest.mark.parametrize("N,K,B,skip", [(1024, 1024, 32, 0), (4096, 2048, 16, 5)])
+# (batches of 16 rows or fewer on shorter outputs run on mma.sync tiles, not
+# on this kernel: both cases keep B > 16)
+@pytest.mark.parametrize("N,K,B,skip", [(1024, 1024, 32, 0), (4096, 2048, 24, 5)])
 def test_gemm_hh_wait_timeout_recovers(cuda_dev, N, K, B, skip):
     """Failure detection on the tensor-core kernel without a GPU fault: the
     test hook makes every TMA producer stop before K-chunk `skip`, so the

@@ -165,11 +165,15 @@ def test_membw_read4_checksum(cuda_dev, swmod):
 
 
 @pytest.mark.parametrize("M,N,K,row0,row1", [(1024, 1024, 2048, 256, 512), (256, 512, 4096, 0, 256),
-                                             (1024, 1024, 1024, 0, 1024)])
+                                             (1024, 1024, 1024, 0, 1024), (2048, 2048, 64, 0, 2048),
+                                             (1152, 1152, 512, 0, 1152), (128, 128, 16, 0, 128)])
 def test_split_k_small_products(cuda_dev, M, N, K, row0, row1):
-    """Products with fewer 128x128 tiles than two per SM split K over CTAs and
-    add the partial tiles in split order: within the FP32 bar of the
-    harness loop, and bit-identical from call to call (deterministic)."""
+    """Products with fewer 128x128 tiles than two per SM run stream-K (equal
+    ranges of the tiles' k-chunks per CTA) and add each tile's pieces in CTA
+    order: within the FP32 bar of the harness loop, and bit-identical from
+    call to call (deterministic).  The cases cover ranges that span two
+    tiles, ranges shorter than one chunk's worth per CTA (K = 64 over 256
+    tiles) and a single whole tile."""
     import torch
     A, B = _mats(M, N, K, 77)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
