@@ -292,12 +292,14 @@ extern "C" __global__ void __launch_bounds__(256, 2)
         u = (long)t * nk + k1;
     }
 }
-// C tile t = the sum, in CTA order, of its pieces in ws.  grid: tiles x 4
-// (a quarter of a tile per CTA); block 256; G = sgemm_b200_stk's grid.
-extern "C" __global__ void sgemm_stk_fixup(const float *__restrict__ ws, float *__restrict__ C, int M, int N, int K,
-                                           int G) {
+// C tile t = the sum, in CTA order, of its pieces in ws.  One float4 of the
+// tile per thread, the loads of up to 8 pieces issued before the adds (a
+// loop of dependent piece loads ran at 1.4 TB/s from L2).  grid: tiles x
+// 16; block 256; G = sgemm_b200_stk's grid.
+extern "C" __global__ void __launch_bounds__(256) sgemm_stk_fixup(const float *__restrict__ ws, float *__restrict__ C,
+                                                                  int M, int N, int K, int G) {
     const int tiles_n = N / SG_BN, tiles = (M / SG_BM) * tiles_n, nk = K / SG_BK;
-    const int t = blockIdx.x / 4, quarter = blockIdx.x % 4;
+    const int t = blockIdx.x / 16, i = (blockIdx.x % 16) * 256 + threadIdx.x;  // float4 index in the tile
     if (t >= tiles) return;
     const long units = (long)tiles * nk, ub = (long)t * nk, ue = ub + nk;
     const int c_lo = stk_owner(units, G, ub), c_hi = stk_owner(units, G, ue - 1);
@@ -305,19 +307,32 @@ extern "C" __global__ void sgemm_stk_fixup(const float *__restrict__ ws, float *
     const int tiles_m = M / SG_BM, per_group = 8 * tiles_n, first_m = (t / per_group) * 8;
     const int gsz = min(tiles_m - first_m, 8);
     const int m0 = (first_m + (t % per_group) % gsz) * SG_BM, n0 = ((t % per_group) / gsz) * SG_BN;
-    for (int i = quarter * 1024 + threadIdx.x; i < (quarter + 1) * 1024; i += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = c_lo; c <= c_hi; c++) {
-            const int piece = (stk_first(units, G, c) / nk == t) ? 0 : 1;
-            const float4 v = reinterpret_cast<const float4 *>(ws + (size_t)(2 * c + piece) * SG_BM * SG_BN)[i];
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+    // every CTA after c_lo starts inside this tile (its piece 0); c_lo's piece
+    // is its second one when it started in an earlier tile
+    const int lo_piece = stk_first(units, G, c_lo) < ub ? 1 : 0;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = c_lo; c0 <= c_hi; c0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int c = c0 + j;
+            v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c <= c_hi) {
+                const int piece = c == c_lo ? lo_piece : 0;
+                v[j] = __ldcg(reinterpret_cast<const float4 *>(ws + (size_t)(2 * c + piece) * SG_BM * SG_BN) + i);
+            }
         }
-        const int r = (i * 4) / SG_BN, col = (i * 4) % SG_BN;
-        *reinterpret_cast<float4 *>(C + (size_t)(m0 + r) * N + n0 + col) = acc;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (c0 + j <= c_hi) {
+                acc.x += v[j].x;
+                acc.y += v[j].y;
+                acc.z += v[j].z;
+                acc.w += v[j].w;
+            }
     }
+    const int r = (i * 4) / SG_BN, col = (i * 4) % SG_BN;
+    *reinterpret_cast<float4 *>(C + (size_t)(m0 + r) * N + n0 + col) = acc;
 }
 
 // One output per thread, k in order, product and sum rounded separately:

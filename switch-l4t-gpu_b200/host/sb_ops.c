@@ -50,7 +50,7 @@ int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K,
         rc = sb_launch(c, F_SGEMM_B200_STK, (unsigned)G, 1, 256, 0, (CUstream)stream, args, 0);
         if (rc) return rc;
         void *fargs[] = {&ws, &cc, (void *)&m, &N, &K, &G};
-        return sb_launch(c, F_SGEMM_STK_FIXUP, (unsigned)(tiles * 4), 1, 256, 0, (CUstream)stream, fargs, 0);
+        return sb_launch(c, F_SGEMM_STK_FIXUP, (unsigned)(tiles * 16), 1, 256, 0, (CUstream)stream, fargs, 0);
     }
     const long grid = tiles < 0x7fffffffL ? tiles : 0x7fffffffL;
     void *args[] = {&a, &b, &cc, (void *)&m, &N, &K};
