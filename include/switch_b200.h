@@ -295,6 +295,28 @@ int sb_engine_profile(sb_engine *e, int which, int reps, void *flush, size_t flu
  * scratch (V floats) may be NULL.  Returns the id, or -1 on bad arguments. */
 int sb_sample_token(const float *logits, int V, const int *ctx, int ctx_len, float temperature, int top_k,
                     float top_p, float rep_penalty, uint32_t *rng_state, float *scratch);
+/* Steps 1-3 of that sampler on the GPU (device pointers): logits[V] FP32,
+ * ctx[ctx_len] token ids.  Writes the top_k candidates -- ids and their
+ * penalised, temperature-scaled values, ordered by value descending then
+ * id ascending, which is the order of the reference's k first-index argmax
+ * passes -- to idx_out / val_out (device).  Bit-identical to the host
+ * steps (IEEE division and multiplication in the same order).  top_k in
+ * 1..64, ceil(V / 1024) * top_k <= 16384; logits finite.  Uses the
+ * context's workspace (calls on different streams must not overlap). */
+int sb_topk_penalized(const float *logits, int V, const int *ctx, int ctx_len, float temperature, float rep_penalty,
+                      int top_k, int *idx_out, float *val_out, void *stream);
+/* Steps 4-6 on the host: softmax of the k candidate values (clamped exp),
+ * top_p prefix, xorshift draw.  idx / val as sb_topk_penalized writes
+ * them (host copies).  Returns the id, or -1 on bad arguments. */
+int sb_sample_topk(const int *idx, const float *val, int top_k, float top_p, uint32_t *rng_state);
+/* The engine's next token from its last step's logits (sb_engine_forward
+ * with want_logits), the first ctx_len token ids it was fed as the
+ * context: sb_topk_penalized on the device, 2 x top_k values copied back,
+ * sb_sample_topk on the host -- the same token as sb_sample_token on the
+ * full logits, without their 608 KB copy.  Returns the id or a negative
+ * SB_ERR_* code. */
+int sb_engine_sample(sb_engine *e, int ctx_len, float temperature, int top_k, float top_p, float rep_penalty,
+                     uint32_t *rng_state);
 
 /* ---- synthetic inputs in the reference layouts -----------------------------
  * Deterministic from `seed`: weights N(0, 0.02) (fp16 round-to-nearest for

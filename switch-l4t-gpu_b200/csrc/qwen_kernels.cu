@@ -396,6 +396,121 @@ extern "C" __global__ void __launch_bounds__(128, 4)
     gemm_hh_mma_body<true, 4>(W, X, Y, K, N, B);
 }
 
+// ---- next-token candidates for the Qwen sampler (qwen_engine.c:375-390):
+// the reference penalises each context id's logit once per occurrence
+// (divide when positive, else multiply), divides every logit by the
+// temperature, then takes k passes of first-index argmax.  The k winners
+// are the first k of all w[i] ordered by (value descending, index
+// ascending), so here each CTA takes the first k of its 1024 ids and one
+// CTA merges them.  The same IEEE operations in the same order give the
+// same w[i] bit for bit; the softmax / top-p / draw over the k values stays
+// on the host (20 values instead of the 608 KB logits vector).
+constexpr int TK_CHUNK = 1024;
+// the better of two candidates: larger value, then smaller index; id < 0 =
+// none
+SB_DEV bool tk_better(float v, int i, float bv, int bi) {
+    return bi < 0 || (i >= 0 && (v > bv || (v == bv && i < bi)));
+}
+SB_DEV void tk_warp_best(float &v, int &i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(SB_FULL, v, o);
+        const int oi = __shfl_xor_sync(SB_FULL, i, o);
+        if (tk_better(ov, oi, v, i)) {
+            v = ov;
+            i = oi;
+        }
+    }
+}
+// k rounds of block argmax over the candidates each thread holds in
+// registers (cv / ci, ci < 0 = empty); writes the winners to out_* in order.
+template <int PER, int NWARP>
+SB_DEV void tk_select(float (&cv)[PER], int (&ci)[PER], int k, int *out_i, float *out_v, float *rv, int *ri) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int r = 0; r < k; r++) {
+        float bv = 0.f;
+        int bi = -1;
+#pragma unroll
+        for (int u = 0; u < PER; u++)
+            if (tk_better(cv[u], ci[u], bv, bi)) {
+                bv = cv[u];
+                bi = ci[u];
+            }
+        tk_warp_best(bv, bi);
+        if (lane == 0) {
+            rv[warp] = bv;
+            ri[warp] = bi;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            bv = lane < NWARP ? rv[lane] : 0.f;
+            bi = lane < NWARP ? ri[lane] : -1;
+            tk_warp_best(bv, bi);
+            if (lane == 0) {
+                out_i[r] = bi;
+                out_v[r] = bv;
+                ri[NWARP] = bi;
+            }
+        }
+        __syncthreads();
+        const int win = ri[NWARP];
+#pragma unroll
+        for (int u = 0; u < PER; u++)
+            if (ci[u] == win) ci[u] = -1;
+        __syncthreads();  // ri / rv are rewritten by the next round
+    }
+}
+// grid ceil(V / 1024), block 256: CTA b's first k of ids [1024 b, 1024 b +
+// 1024) -> cand_*[b * k ..]; empty slots get id -1.  k <= 64.
+extern "C" __global__ void __launch_bounds__(256) topk_partial(const float *__restrict__ logits, int V,
+                                                               const int *__restrict__ ctx, int ctx_len,
+                                                               float temperature, float rep_penalty, int k,
+                                                               int *__restrict__ cand_i, float *__restrict__ cand_v) {
+    __shared__ int cnt[TK_CHUNK];
+    __shared__ float rv[8];
+    __shared__ int ri[9];
+    const int i0 = blockIdx.x * TK_CHUNK, n = min(TK_CHUNK, V - i0);
+    for (int j = threadIdx.x; j < TK_CHUNK; j += blockDim.x) cnt[j] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < ctx_len; p += blockDim.x) {
+        const int t = ctx[p];
+        if (t >= i0 && t < i0 + n) atomicAdd(&cnt[t - i0], 1);
+    }
+    __syncthreads();
+    float cv[4];
+    int ci[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int j = threadIdx.x + 256 * u;
+        ci[u] = -1;
+        cv[u] = 0.f;
+        if (j < n) {
+            float v = logits[i0 + j];
+            for (int c = cnt[j]; c > 0; c--) v = v > 0.f ? __fdiv_rn(v, rep_penalty) : __fmul_rn(v, rep_penalty);
+            cv[u] = __fdiv_rn(v, temperature);
+            ci[u] = i0 + j;
+        }
+    }
+    tk_select<4, 8>(cv, ci, k, cand_i + (size_t)blockIdx.x * k, cand_v + (size_t)blockIdx.x * k, rv, ri);
+}
+// one CTA of 1024 threads: the first k of the ncand (<= 16384) partial
+// candidates -> out_*[0 .. k).
+extern "C" __global__ void __launch_bounds__(1024) topk_merge(const int *__restrict__ cand_i,
+                                                              const float *__restrict__ cand_v, int ncand, int k,
+                                                              int *__restrict__ out_i, float *__restrict__ out_v) {
+    __shared__ float rv[32];
+    __shared__ int ri[33];
+    float cv[16];
+    int ci[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int j = threadIdx.x + 1024 * u;
+        ci[u] = j < ncand ? cand_i[j] : -1;
+        cv[u] = j < ncand ? cand_v[j] : 0.f;
+    }
+    tk_select<16, 32>(cv, ci, k, out_i, out_v, rv, ri);
+}
+
 // GQA decode attention with an explicit T (no step state); 7 query heads
 // per KV head.  grid (NKV, max_splits), block SB_ATTN_THREADS.
 extern "C" __global__ void attn_decode_g7(const float *__restrict__ q, const float *__restrict__ kc,

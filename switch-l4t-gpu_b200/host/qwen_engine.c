@@ -52,21 +52,30 @@ static void gpu_forward(sb_engine *e, int token, int pos, int want_logits, float
     else if (sb_engine_forward(e, token, pos, want_logits, logits)) cli_die("forward");
 }
 
+/* The next token after a step whose logits are on the device (the engine
+ * path: the top-20 candidates are picked there, the draw is on the host)
+ * or in scratch_logits (the --ptx module path). */
 static int next_token(sb_engine *e, const int *ids, int n) {
-    (void)e;
-    if (greedy_mode) return cli_argmax(scratch_logits, V);
+    if (greedy_mode) return cli_argmax(scratch_logits, V); /* only reached on the --ptx path */
+    if (!modpath) {
+        const int t = sb_engine_sample(e, n, 0.7f, 20, 0.8f, 1.1f, &rng_state);
+        if (t < 0) cli_die("sample");
+        return t;
+    }
     return sb_sample_token(scratch_logits, V, ids, n, 0.7f, 20, 0.8f, 1.1f, &rng_state, sample_scratch);
 }
 
-/* Sampled generation: forward per token with host logits. Returns total. */
+/* Sampled generation: one forward per token; the engine keeps the logits
+ * on the device. Returns total. */
 static int generate_sampled(sb_engine *e, int *ids, int total, int n_gen, int cap, int *emitted) {
-    for (int p = 0; p < total; p++) gpu_forward(e, ids[p], p, p == total - 1, p == total - 1 ? scratch_logits : NULL);
+    float *host_logits = modpath ? scratch_logits : NULL;
+    for (int p = 0; p < total; p++) gpu_forward(e, ids[p], p, p == total - 1, p == total - 1 ? host_logits : NULL);
     int nxt = next_token(e, ids, total);
     ids[total++] = nxt;
     *emitted = 0;
     for (int g = 0; g < n_gen && total < cap; g++) {
         if (nxt == EOT || nxt == IM_END) break;
-        gpu_forward(e, nxt, total - 1, 1, scratch_logits);
+        gpu_forward(e, nxt, total - 1, 1, host_logits);
         nxt = next_token(e, ids, total);
         ids[total++] = nxt;
         (*emitted)++;

@@ -41,6 +41,7 @@ struct sb_engine {
     CUdeviceptr kv; /* [2][NL][ctx][kvw] */
     CUdeviceptr scratch;
     CUdeviceptr x, q, att, hid, logits, part, counters, step, tokens;
+    CUdeviceptr tk; /* sampler candidates: 64 ids then 64 values */
     int max_splits;
     int V, NL, kvw;
     CUgraphExec gexec[2];
@@ -397,6 +398,7 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     CARVE(ll, e->ll_words * 8);
     CARVE(sync, 8);
     CARVE(err, 4);
+    CARVE(tk, 64 * 8);
 #undef CARVE
     if (cuMemAlloc(&e->scratch, off)) { sb_fail(SB_ERR_STATE, "scratch allocation", __FILE__, __LINE__); goto fail; }
     e->x += e->scratch; e->q += e->scratch; e->att += e->scratch; e->hid += e->scratch;
@@ -405,6 +407,7 @@ sb_engine *sb_engine_create(int model, const char *weights_path, int max_ctx, un
     e->ll += e->scratch;
     e->sync += e->scratch;
     e->err += e->scratch;
+    e->tk += e->scratch;
     if (cuMemsetD8Async(e->scratch, 0, off, e->stream) || cuMemsetD8Async(e->kv, 0, kv_bytes, e->stream) ||
         cuStreamSynchronize(e->stream)) {
         sb_fail(SB_ERR_STATE, "initialisation", __FILE__, __LINE__);
@@ -797,6 +800,26 @@ const char *sb_engine_step_kernel(sb_engine *e) {
 }
 
 int sb_engine_uses_persistent_kernel(sb_engine *e) { return e && e->mk; }
+
+int sb_engine_sample(sb_engine *e, int ctx_len, float temperature, int top_k, float top_p, float rep_penalty,
+                     uint32_t *rng_state) {
+    if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);
+    SB_ARG(ctx_len >= 0 && ctx_len <= e->ctx_cap && rng_state, "bad sampling arguments");
+    SB_ARG(top_k >= 1 && top_k <= 64, "top_k must be in 1..64");
+    /* the device picks the k candidates of the reference's steps 1-3 from
+     * the step's logits and the token ids in the KV order; the host draws */
+    CUdeviceptr ci = e->tk, cv = e->tk + 64 * 4;
+    int rc = sb_topk_penalized((const float *)(uintptr_t)e->logits, e->V, (const int *)(uintptr_t)e->tokens, ctx_len,
+                               temperature, rep_penalty, top_k, (int *)(uintptr_t)ci, (float *)(uintptr_t)cv,
+                               e->stream);
+    if (rc) return -rc;
+    int idx[64];
+    float val[64];
+    SB_CK(cuMemcpyDtoHAsync(idx, ci, (size_t)top_k * 4, e->stream));
+    SB_CK(cuMemcpyDtoHAsync(val, cv, (size_t)top_k * 4, e->stream));
+    SB_CK(cuStreamSynchronize(e->stream));
+    return sb_sample_topk(idx, val, top_k, top_p, rng_state);
+}
 
 int sb_engine_set_test_stall(sb_engine *e, int cta) {
     if (!e) return sb_fail(SB_ERR_ARG, "null engine", __FILE__, __LINE__);

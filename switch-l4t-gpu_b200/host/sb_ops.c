@@ -436,3 +436,26 @@ int sb_tc_error(int *err) {
     if (*err) SB_CK(cuMemsetD32(p, 0, 1));
     return 0;
 }
+
+/* ---------------------------------------------------------- token selection */
+int sb_topk_penalized(const float *logits, int V, const int *ctx, int ctx_len, float temperature, float rep_penalty,
+                      int top_k, int *idx_out, float *val_out, void *stream) {
+    SB_ARG(logits && V > 0 && ctx_len >= 0 && (ctx || ctx_len == 0) && idx_out && val_out, "bad top-k arguments");
+    SB_ARG(top_k >= 1 && top_k <= 64 && temperature > 0.0f && rep_penalty > 0.0f, "bad top-k settings");
+    const long G = CEIL_DIV(V, 1024);
+    SB_ARG(G * top_k <= 16384, "ceil(V / 1024) x top_k exceeds 16384 candidates");
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    CUdeviceptr ws;
+    int rc = ws_reserve(c, (size_t)G * top_k * 8, &ws);
+    if (rc) return rc;
+    CUdeviceptr lg = DP(logits), cx = DP(ctx), ci = ws, cv = ws + (size_t)G * top_k * 4;
+    void *args[] = {&lg, &V, &cx, &ctx_len, &temperature, &rep_penalty, &top_k, &ci, &cv};
+    rc = sb_launch(c, F_TOPK_PARTIAL, (unsigned)G, 1, 256, 0, (CUstream)stream, args, 0);
+    if (rc) return rc;
+    int ncand = (int)(G * top_k);
+    CUdeviceptr oi = DP(idx_out), ov = DP(val_out);
+    void *margs[] = {&ci, &cv, &ncand, &top_k, &oi, &ov};
+    return sb_launch(c, F_TOPK_MERGE, 1, 1, 1024, 0, (CUstream)stream, margs, 0);
+}
+

@@ -42,6 +42,8 @@ static const struct {
     [F_GEMM_HH_MMA16] = {M_QWEN, "gemm_hh_mma16"},
     [F_GEMM_HH_MMA8_W4] = {M_QWEN, "gemm_hh_mma8_w4"},
     [F_GEMM_HH_MMA16_W4] = {M_QWEN, "gemm_hh_mma16_w4"},
+    [F_TOPK_PARTIAL] = {M_QWEN, "topk_partial"},
+    [F_TOPK_MERGE] = {M_QWEN, "topk_merge"},
     [F_SGEMM_NAIVE] = {M_SWITCH, "sgemm_naive"},
     [F_MEMBW] = {M_SWITCH, "membw_read4"},
     [F_FMA_PEAK] = {M_SWITCH, "fma_peak"},

@@ -54,10 +54,18 @@ int sb_sample_token(const float *logits, int V, const int *ctx, int ctx_len, flo
         val[k] = w[b];
         w[b] = -1e30f;
     }
-    const float mx = val[0];
+    if (!scratch) free(w);
+    return sb_sample_topk(idx, val, top_k, top_p, rng_state);
+}
+
+/* steps 4-6 on the k candidates (idx, value) of steps 1-3, in order */
+int sb_sample_topk(const int *idx, const float *topv, int top_k, float top_p, uint32_t *rng_state) {
+    if (!idx || !topv || top_k <= 0 || top_k > 64 || !rng_state) return -1;
+    float val[64];
+    const float mx = topv[0];
     float sum = 0.0f;
     for (int k = 0; k < top_k; k++) {
-        val[k] = clamped_exp(val[k] - mx);
+        val[k] = clamped_exp(topv[k] - mx);
         sum += val[k];
     }
     for (int k = 0; k < top_k; k++) val[k] /= sum;
@@ -80,6 +88,5 @@ int sb_sample_token(const float *logits, int V, const int *ctx, int ctx_len, flo
             break;
         }
     }
-    if (!scratch) free(w);
     return out;
 }

@@ -120,6 +120,10 @@ def lib():
     _sig(L.sb_engine_set_trace, I, P, P)
     _sig(L.sb_engine_set_test_stall, I, P, I)
     _sig(L.sb_engine_profile, I, P, I, I, P, ctypes.c_size_t, ctypes.POINTER(F), ctypes.POINTER(D))
+    _sig(L.sb_sample_token, I, P, I, P, I, F, I, F, F, ctypes.POINTER(ctypes.c_uint32), P)
+    _sig(L.sb_topk_penalized, I, P, I, P, I, F, F, I, P, P, P)
+    _sig(L.sb_sample_topk, I, P, P, I, F, ctypes.POINTER(ctypes.c_uint32))
+    _sig(L.sb_engine_sample, I, P, I, F, I, F, F, ctypes.POINTER(ctypes.c_uint32))
     _sig(L.sb_synth_weights, ctypes.c_long, I, ctypes.c_char_p, U64)
     _sig(L.sb_synth_ids, None, P, I, I, U64)
     _sig(L.sb_synth_uniform, None, P, ctypes.c_size_t, F, F, U64)
@@ -213,6 +217,22 @@ def gemv_hh(W, X, Y, K, N, B, stream=None):
 def gemm_hh(W, X, Y, K, N, B, stream=None):
     """Tensor-core (tcgen05) Y[b][n] = sum_k W[n][k] X[b][k], B <= 256."""
     check(lib().sb_gemm_hh(_p(W), _p(X), _p(Y), K, N, B, _s(stream)))
+
+
+def topk_penalized(logits, V, ctx, ctx_len, temperature, rep_penalty, k, idx_out, val_out, stream=None):
+    """Device steps 1-3 of the Qwen sampler: the k (id, value) candidates of
+    the penalised, temperature-scaled logits (all device tensors)."""
+    check(lib().sb_topk_penalized(_p(logits), V, _p(ctx), ctx_len, temperature, rep_penalty, k, _p(idx_out),
+                                  _p(val_out), _s(stream)))
+
+
+def sample_topk(idx, val, top_p, state):
+    """Host steps 4-6 on k candidates (numpy int32 / float32 arrays); state:
+    ctypes.c_uint32 xorshift state, advanced in place."""
+    import numpy as np
+    idx = np.ascontiguousarray(idx, dtype=np.int32)
+    val = np.ascontiguousarray(val, dtype=np.float32)
+    return lib().sb_sample_topk(idx.ctypes.data, val.ctypes.data, len(idx), top_p, ctypes.byref(state))
 
 
 def sgemm_3xtf32(A, B, C, M, N, K, stream=None):
@@ -319,6 +339,14 @@ class Engine:
         """Reference gpu_forward contract; logits_out: numpy float32[V] or None."""
         ptr = None if logits_out is None else logits_out.ctypes.data
         check(lib().sb_engine_forward(self.h, token, pos, 1 if want_logits else 0, ptr))
+
+    def sample(self, ctx_len, state, temperature=0.7, top_k=20, top_p=0.8, rep_penalty=1.1):
+        """Next token from the last step's device logits with the reference
+        sampler's settings (device top-k, host draw); state: ctypes.c_uint32."""
+        t = lib().sb_engine_sample(self.h, ctx_len, temperature, top_k, top_p, rep_penalty, ctypes.byref(state))
+        if t < 0:
+            check(-t)
+        return t
 
     def generate(self, prompt, n_gen, stop_eos=False):
         n_prompt = len(prompt)

@@ -54,3 +54,25 @@ def test_sampler_matches_reference_256_draws():
         ctx.append(int(got))
     # the draws were not all the top candidate: the distribution was sampled
     assert len(set(ctx[32:])) > 16
+
+
+@pytest.mark.skipif(not orc.ref_available(), reason="oracle/_ref not built (needs the reference sources)")
+def test_topk_restatement_and_host_draw_match_reference():
+    """The float32 restatement of steps 1-3 that the GPU sampler test uses
+    as its oracle, followed by sb_sample_topk (steps 4-6), draws what the
+    reference's sample_token draws: 64 consecutive draws."""
+    from test_gpu_sampler import _host_topk, _logits
+    ref = orc.ref_lib("qwen")
+    ref.ref_sampler_seed(1234)
+    state = ctypes.c_uint32(1234)
+    rng = np.random.default_rng(5)
+    ctx = [int(t) for t in sb200.synth_ids(32, V, 1000)]
+    for step in range(64):
+        w = _logits(rng, ctx)
+        c = np.asarray(ctx, dtype=np.int32)
+        want = ref.ref_sample_token(w.ctypes.data_as(ctypes.c_void_p), c.ctypes.data_as(ctypes.c_void_p), len(ctx))
+        idx, val = _host_topk(w, ctx, 20)
+        got = sb200.sample_topk(idx, val, 0.8, state)
+        assert got == want, f"draw {step}: {got} against the reference's {want}"
+        ctx.append(int(got))
+

@@ -82,6 +82,60 @@ def test_engine_cli_greedy_out_ids(cuda_dev, qwen_weights, gpt2_weights, tmp_pat
     assert _read_ids(tmp_path / "out.ids") == _oracle_greedy(model, w, V, prompt, 10, eos)
 
 
+def test_qwen_cli_sampled_out_ids(cuda_dev, qwen_weights, tmp_path):
+    """Without --greedy the engine samples with the reference's settings
+    (qwen_engine.c:375-399: penalty 1.1, temperature 0.7, top-k 20, top-p
+    0.8, xorshift seeded 1234), its top-20 picked on the device.  out.ids
+    equals the reference's prime-then-sample loop run on the same engine's
+    logits (copied to the host each step) and drawn by the reference's own
+    sample_token where oracle/_ref is built (else by sb_sample_token, which
+    tests/test_cpu_sampler.py pins to it).  The logits themselves are
+    checked against the oracle in tests/test_gpu_engine.py; sampling from
+    CPU-oracle logits instead would make the comparison depend on near-ties
+    among the top candidates."""
+    import ctypes
+
+    V = sb200.QWEN["V"]
+    prompt = sb200.synth_ids(9, V, 778)
+    _write_ids(tmp_path / "p.ids", prompt)
+    out = subprocess.run([os.path.join(BIN, "qwen_engine"), "--weights", str(qwen_weights), "--ids", "p.ids", "--gen",
+                          "12", "--ctx", "128"], capture_output=True, text=True, timeout=300, cwd=tmp_path)
+    assert out.returncode == 0, out.stderr[-800:]
+    got = _read_ids(tmp_path / "out.ids")
+    if orc.ref_available():
+        refl = orc.ref_lib("qwen")
+        refl.ref_sampler_seed(1234)
+
+        def draw(logits, ids):
+            c = np.asarray(ids, dtype=np.int32)
+            return refl.ref_sample_token(logits.ctypes.data_as(ctypes.c_void_p), c.ctypes.data_as(ctypes.c_void_p),
+                                         len(ids))
+    else:
+        state, scratch = ctypes.c_uint32(1234), np.zeros(V, dtype=np.float32)
+
+        def draw(logits, ids):
+            c = np.asarray(ids, dtype=np.int32)
+            return sb200.lib().sb_sample_token(logits.ctypes.data, V, c.ctypes.data, len(ids), 0.7, 20, 0.8, 1.1,
+                                               ctypes.byref(state), scratch.ctypes.data)
+    e = sb200.Engine(sb200.MODEL_QWEN, qwen_weights, 128)
+    try:
+        ids, logits = list(prompt), np.zeros(V, dtype=np.float32)
+        for p, t in enumerate(prompt):
+            e.forward(t, p, p == len(prompt) - 1, logits if p == len(prompt) - 1 else None)
+        nxt = draw(logits, ids)
+        ids.append(nxt)
+        for _ in range(12):
+            if nxt in QW_EOS:
+                break
+            e.forward(nxt, len(ids) - 1, True, logits)
+            nxt = draw(logits, ids)
+            ids.append(nxt)
+    finally:
+        e.close()
+    assert got == ids
+    assert len(set(got[9:])) > 3  # sampled, not a repeated argmax
+
+
 def test_gemv_test_cli(cuda_dev):
     """gemv_test <module> N K: every kernel of the M0 module CORRECT against
     the harness's CPU loop, then GEMV_TEST_DONE."""
