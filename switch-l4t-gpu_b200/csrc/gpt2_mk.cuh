@@ -301,7 +301,7 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
                     vv[k] = __ldcg(reinterpret_cast<const float2 *>(vc + (long)t * C + h * HD) + lane);
                 }
             }
-            float2 *qkv_s = reinterpret_cast<float2 *>(opart);
+            float2 *qkv_s = reinterpret_cast<float2 *>(xs);  // free until S3 writes the attention output
             bool ok = true;
             if (warp == 0) {  // q (and the current k, v) requested together: one round trip
                 const bool cur = t1 == T;
@@ -353,20 +353,17 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
                 const float d = warp_sum(fmaf(q2.x, k2.x, q2.y * k2.y)) * 0.125f;
                 if (lane == 0) scores[j] = d;
             }
+            // each warp keeps its own softmax (max, sum, P.V); the CTA combines
+            // the sixteen once
             float wm = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
             __syncwarp();
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) wm = fmaxf(wm, scores[j]);
-            if (lane == 0) wmax_s[warp] = wm;
-            if (__syncthreads_or(!ok)) { aborted = true; break; }
-            float m = -1e30f;
-#pragma unroll
-            for (int w = 0; w < WARPS; w++) m = fmaxf(m, wmax_s[w]);
             float lsum = 0.f;
             float2 o = make_float2(0.f, 0.f);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 if (warp + WARPS * k < n) {
-                    const float e = expf(sc[k] - m);
+                    const float e = expf(sc[k] - wm);
                     lsum += e;
                     o.x = fmaf(e, vv[k].x, o.x);
                     o.y = fmaf(e, vv[k].y, o.y);
@@ -374,32 +371,39 @@ extern "C" __global__ void __launch_bounds__(g2mk::THREADS, 1) gpt2_decode_mk(co
             }
             for (int j = warp + 4 * WARPS; j < n; j += WARPS) {
                 const int t = t0 + j;
-                const float e = expf(scores[j] - m);
+                const float e = expf(scores[j] - wm);
                 lsum += e;
                 const float2 v2 = t == pos ? vpos : __ldcg(reinterpret_cast<const float2 *>(vc + (long)t * C + h * HD) + lane);
                 o.x = fmaf(e, v2.x, o.x);
                 o.y = fmaf(e, v2.y, o.y);
             }
-            __syncthreads();  // every warp has read q/k/v from qkv_s (opart) before it is overwritten
             reinterpret_cast<float2 *>(opart + warp * HD)[lane] = o;
-            if (lane == 0) ksum[warp] = lsum;
+            if (lane == 0) {
+                ksum[warp] = lsum;
+                wmax_s[warp] = wm;
+            }
             __syncthreads();
             if (tid < HD) {
-                float acc = 0.f;
+                float M = -1e30f;
 #pragma unroll
-                for (int w = 0; w < WARPS; w++) acc += opart[w * HD + tid];
+                for (int w = 0; w < WARPS; w++) M = fmaxf(M, wmax_s[w]);
+                float acc = 0.f, ls = 0.f;
+#pragma unroll
+                for (int w = 0; w < WARPS; w++) {
+                    const float f = expf(wmax_s[w] - M);
+                    acc = fmaf(f, opart[w * HD + tid], acc);
+                    ls = fmaf(f, ksum[w], ls);
+                }
                 u64 *pw = llpart + (long)(h * SPLITS_MAX + s) * PW;
                 const unsigned e = epoch(l, 1);
                 ll_put(pw + tid, acc, e);
                 if (tid == 0) {
-                    float ls = 0.f;
-#pragma unroll
-                    for (int w = 0; w < WARPS; w++) ls += ksum[w];
-                    ll_put(pw + HD, m, e);
+                    ll_put(pw + HD, M, e);
                     ll_put(pw + HD + 1, ls, e);
                 }
             }
-            __syncthreads();
+            // (the next item's first barrier, or S3's poll barrier, orders
+            // the combine's reads before opart / ksum are rewritten)
         }
         if (aborted) break;
         stamp(l, 1, 1);

@@ -145,6 +145,7 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
     unsigned *xhw = reinterpret_cast<unsigned *>(xh4), *xlw = reinterpret_cast<unsigned *>(xl4);
     unsigned short *xhs = reinterpret_cast<unsigned short *>(xh4), *xls = reinterpret_cast<unsigned short *>(xl4);
     __shared__ float wmax_s[WARPS], xown[8], gu_s[2 * HID_MAX];
+    __shared__ float wgt_s[NH * SPLITS_MAX];  // S3: softmax weight of each (head, split) partial
     __shared__ unsigned hid_hl[HID_MAX];
     __shared__ float qkv_o[8][2];  // S1: this CTA's pair outputs (rows r, r + 32)
     __shared__ unsigned long long best_s;
@@ -537,18 +538,24 @@ extern "C" __global__ void __launch_bounds__(qmk::THREADS, 1) qwen_decode_mk2(co
             }
             if (__syncthreads_or(!ok)) { aborted = true; break; }
             stamp(l, 2, 0);
+            // each (head, split) weight once, not once per output element
+            if (tid < NH * nsplit) {
+                const int h = tid / nsplit;
+                float M = -1e30f;
+                for (int s = 0; s < nsplit; s++) M = fmaxf(M, mlv[2 * (h * nsplit + s)]);
+                wgt_s[tid] = expf(mlv[2 * tid] - M);
+            }
+            __syncthreads();
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const int d = tid + THREADS * u;
                 if (d >= C) break;
                 const int h = d / HD;
-                float M = -1e30f;
-                for (int s = 0; s < nsplit; s++) M = fmaxf(M, mlv[2 * (h * nsplit + s)]);
                 float acc = 0.f, Lsum = 0.f;
 #pragma unroll
                 for (int s = 0; s < SPLITS_MAX; s++) {
                     if (s < nsplit) {
-                        const float wgt = expf(mlv[2 * (h * nsplit + s)] - M);
+                        const float wgt = wgt_s[h * nsplit + s];
                         Lsum = fmaf(wgt, mlv[2 * (h * nsplit + s) + 1], Lsum);
                         acc = fmaf(wgt, ov[u][s], acc);
                     }
