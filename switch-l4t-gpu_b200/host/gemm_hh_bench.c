@@ -1,5 +1,6 @@
-/* gemm_hh_bench.c -- batched FP16 GEMM (sb_gemm_hh, tcgen05 tensor cores)
- * or GEMV (sb_gemv_hh, CUDA cores, B <= 8) check + bandwidth harness:
+/* gemm_hh_bench.c -- batched FP16 GEMM (sb_gemm_hh: tcgen05 tensor cores,
+ * or mma.sync tiles for batches <= 16 on short outputs) or GEMV
+ * (sb_gemv_hh, CUDA cores, B <= 8) check + bandwidth harness:
  *
  *   gemm_hh_bench N K B [reps] [--cuda-core]
  *
