@@ -301,7 +301,7 @@ int sb_sample_token(const float *logits, int V, const int *ctx, int ctx_len, flo
  * id ascending, which is the order of the reference's k first-index argmax
  * passes -- to idx_out / val_out (device).  Bit-identical to the host
  * steps (IEEE division and multiplication in the same order).  top_k in
- * 1..64, ceil(V / 1024) * top_k <= 16384; logits finite.  Uses the
+ * 1..64, V <= 2^18, ceil(V / 1024) * top_k <= 16384; logits finite.  Uses the
  * context's workspace (calls on different streams must not overlap). */
 int sb_topk_penalized(const float *logits, int V, const int *ctx, int ctx_len, float temperature, float rep_penalty,
                       int top_k, int *idx_out, float *val_out, void *stream);

@@ -405,110 +405,185 @@ extern "C" __global__ void __launch_bounds__(128, 4)
 // CTA merges them.  The same IEEE operations in the same order give the
 // same w[i] bit for bit; the softmax / top-p / draw over the k values stays
 // on the host (20 values instead of the 608 KB logits vector).
+//
+// No sorting network: every step ranks a small candidate set.  A candidate
+// is a 64-bit key -- the value's bits mapped to an order-preserving
+// unsigned (-0 taken as +0: the reference's comparisons treat them as
+// equal) above an id rank that is larger for a smaller id -- so keys are
+// distinct and a larger key is a better candidate; 0 = empty.  The first k
+// of a set S are the keys whose rank (the number of larger keys in S) is
+// below k.  A lower bound T of the k-th best key shrinks S first: the k-th
+// best of per-thread (or per-list) maxima is one, since k holders each
+// have a key at least that good; then at most 4k keys (k lists x k in the
+// merge) reach T.  (Bitonic networks -- block-wide or in one warp's
+// registers -- took 13 and 18 us: latency chains on one SM.)
 constexpr int TK_CHUNK = 1024;
-// the better of two candidates: larger value, then smaller index; id < 0 =
-// none
-SB_DEV bool tk_better(float v, int i, float bv, int bi) {
-    return bi < 0 || (i >= 0 && (v > bv || (v == bv && i < bi)));
+SB_DEV unsigned tk_ord(float v) {
+    const unsigned u = __float_as_uint(v == 0.f ? 0.f : v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
-SB_DEV void tk_warp_best(float &v, int &i) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(SB_FULL, v, o);
-        const int oi = __shfl_xor_sync(SB_FULL, i, o);
-        if (tk_better(ov, oi, v, i)) {
-            v = ov;
-            i = oi;
-        }
+// key of (value, id) with `low` (< 2^14) in the lowest bits; ids < 2^18
+SB_DEV unsigned long long tk_key(float v, int id, int low) {
+    return ((unsigned long long)tk_ord(v) << 32) | ((unsigned)(0x3FFFF - id) << 14) | (unsigned)low;
+}
+// the first k of the n keys in s (all distinct on bits 14 and up, since
+// they differ in value or id): out(rank, key) for each key whose rank < k
+template <typename F>
+SB_DEV void tk_rank(const unsigned long long *s, int n, int k, F out) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long me = s[i] >> 14;
+        int r = 0;
+        for (int j = 0; j < n; j++) r += (s[j] >> 14) > me;
+        if (r < k) out(r, s[i]);
     }
 }
-// k rounds of block argmax over the candidates each thread holds in
-// registers (cv / ci, ci < 0 = empty); writes the winners to out_* in order.
-template <int PER, int NWARP>
-SB_DEV void tk_select(float (&cv)[PER], int (&ci)[PER], int k, int *out_i, float *out_v, float *rv, int *ri) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int r = 0; r < k; r++) {
-        float bv = 0.f;
-        int bi = -1;
-#pragma unroll
-        for (int u = 0; u < PER; u++)
-            if (tk_better(cv[u], ci[u], bv, bi)) {
-                bv = cv[u];
-                bi = ci[u];
-            }
-        tk_warp_best(bv, bi);
-        if (lane == 0) {
-            rv[warp] = bv;
-            ri[warp] = bi;
-        }
-        __syncthreads();
-        if (warp == 0) {
-            bv = lane < NWARP ? rv[lane] : 0.f;
-            bi = lane < NWARP ? ri[lane] : -1;
-            tk_warp_best(bv, bi);
-            if (lane == 0) {
-                out_i[r] = bi;
-                out_v[r] = bv;
-                ri[NWARP] = bi;
-            }
-        }
-        __syncthreads();
-        const int win = ri[NWARP];
-#pragma unroll
-        for (int u = 0; u < PER; u++)
-            if (ci[u] == win) ci[u] = -1;
-        __syncthreads();  // ri / rv are rewritten by the next round
-    }
+// one shared atomic per warp: returns this lane's slot (or -1) for `keep`
+SB_DEV int tk_append(bool keep, int *count) {
+    const int lane = threadIdx.x & 31;
+    const unsigned ball = __ballot_sync(SB_FULL, keep);
+    int base = 0;
+    if (lane == 0 && ball) base = atomicAdd(count, __popc(ball));
+    base = __shfl_sync(SB_FULL, base, 0);
+    return keep ? base + __popc(ball & ((1u << lane) - 1u)) : -1;
 }
 // grid ceil(V / 1024), block 256: CTA b's first k of ids [1024 b, 1024 b +
-// 1024) -> cand_*[b * k ..]; empty slots get id -1.  k <= 64.
+// 1024) -> cand_*[b * k ..] in order; empty slots get id -1.  k <= 64.
 extern "C" __global__ void __launch_bounds__(256) topk_partial(const float *__restrict__ logits, int V,
                                                                const int *__restrict__ ctx, int ctx_len,
                                                                float temperature, float rep_penalty, int k,
                                                                int *__restrict__ cand_i, float *__restrict__ cand_v) {
     __shared__ int cnt[TK_CHUNK];
-    __shared__ float rv[8];
-    __shared__ int ri[9];
+    __shared__ float w[TK_CHUNK];
+    __shared__ unsigned long long tmax[256], surv[4 * 64];
+    __shared__ unsigned long long thr;
+    __shared__ int nsurv;
     const int i0 = blockIdx.x * TK_CHUNK, n = min(TK_CHUNK, V - i0);
+    float lg[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {  // issued before the context scan
+        const int j = threadIdx.x + 256 * r;
+        lg[r] = j < n ? logits[i0 + j] : 0.f;
+    }
     for (int j = threadIdx.x; j < TK_CHUNK; j += blockDim.x) cnt[j] = 0;
+    if (threadIdx.x == 0) {
+        thr = 0ull;
+        nsurv = 0;
+    }
     __syncthreads();
     for (int p = threadIdx.x; p < ctx_len; p += blockDim.x) {
         const int t = ctx[p];
         if (t >= i0 && t < i0 + n) atomicAdd(&cnt[t - i0], 1);
     }
     __syncthreads();
-    float cv[4];
-    int ci[4];
+    unsigned long long key[4], mx = 0ull;
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-        const int j = threadIdx.x + 256 * u;
-        ci[u] = -1;
-        cv[u] = 0.f;
+    for (int r = 0; r < 4; r++) {
+        const int j = threadIdx.x + 256 * r;
+        key[r] = 0ull;
         if (j < n) {
-            float v = logits[i0 + j];
+            float v = lg[r];
             for (int c = cnt[j]; c > 0; c--) v = v > 0.f ? __fdiv_rn(v, rep_penalty) : __fmul_rn(v, rep_penalty);
-            cv[u] = __fdiv_rn(v, temperature);
-            ci[u] = i0 + j;
+            v = __fdiv_rn(v, temperature);
+            w[j] = v;
+            key[r] = tk_key(v, i0 + j, j);
+            mx = key[r] > mx ? key[r] : mx;
         }
     }
-    tk_select<4, 8>(cv, ci, k, cand_i + (size_t)blockIdx.x * k, cand_v + (size_t)blockIdx.x * k, rv, ri);
+    tmax[threadIdx.x] = mx;
+    __syncthreads();
+    if (mx) {  // T = the k-th best thread maximum
+        int r = 0;
+        for (int t = 0; t < 256; t++) r += tmax[t] > mx;
+        if (r == k - 1) thr = mx;
+    }
+    __syncthreads();
+    const unsigned long long T = thr;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int pos = tk_append(key[r] && key[r] >= T, &nsurv);
+        if (pos >= 0) surv[pos] = key[r];
+    }
+    __syncthreads();
+    const int ns = nsurv;  // <= 4 k: only threads whose maximum reached T hold survivors
+    int *ci = cand_i + (size_t)blockIdx.x * k;
+    float *cv = cand_v + (size_t)blockIdx.x * k;
+    tk_rank(surv, ns, k, [&](int r, unsigned long long kk) {
+        const int j = (int)(kk & 0x3FFFu);
+        ci[r] = i0 + j;
+        cv[r] = w[j];
+    });
+    for (int r = ns + threadIdx.x; r < k; r += blockDim.x) {
+        ci[r] = -1;
+        cv[r] = 0.f;
+    }
 }
 // one CTA of 1024 threads: the first k of the ncand (<= 16384) partial
-// candidates -> out_*[0 .. k).
+// candidates (ids < 2^18; G = ncand / k <= 256 lists of k, each in order)
+// -> out_*[0 .. k).  Every candidate is loaded once, all loads issued
+// together.  T = the larger of two lower bounds of the k-th best key: the
+// k-th best of the G lists' first keys, and each list's k-th key; at most
+// k lists have a first key >= T, so at most k * k candidates are ranked.
 extern "C" __global__ void __launch_bounds__(1024) topk_merge(const int *__restrict__ cand_i,
                                                               const float *__restrict__ cand_v, int ncand, int k,
                                                               int *__restrict__ out_i, float *__restrict__ out_v) {
-    __shared__ float rv[32];
-    __shared__ int ri[33];
-    float cv[16];
-    int ci[16];
+    __shared__ unsigned long long surv[4096], first[256];
+    __shared__ unsigned long long thr;
+    __shared__ int nsurv;
+    const int G = ncand / k, lane = threadIdx.x & 31;
+    constexpr int PER = 16;  // candidates per thread (ncand <= 16384)
+    unsigned long long key[PER];
 #pragma unroll
-    for (int u = 0; u < 16; u++) {
+    for (int u = 0; u < PER; u++) {
         const int j = threadIdx.x + 1024 * u;
-        ci[u] = j < ncand ? cand_i[j] : -1;
-        cv[u] = j < ncand ? cand_v[j] : 0.f;
+        const int id = j < ncand ? cand_i[j] : -1;
+        const float v = j < ncand ? cand_v[j] : 0.f;
+        key[u] = id >= 0 ? tk_key(v, id, j) : 0ull;
     }
-    tk_select<16, 32>(cv, ci, k, out_i, out_v, rv, ri);
+    if (threadIdx.x == 0) {
+        thr = 0ull;
+        nsurv = 0;
+    }
+    if (threadIdx.x < 256) first[threadIdx.x] = 0ull;
+    __syncthreads();
+    unsigned long long kth = 0ull;
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+        const int j = threadIdx.x + 1024 * u;
+        if (!key[u]) continue;
+        if (j % k == k - 1 && key[u] > kth) kth = key[u];  // a list's k-th key
+        if (j % k == 0) first[j / k] = key[u];            // a list's first key
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ob = __shfl_xor_sync(SB_FULL, kth, o);
+        kth = ob > kth ? ob : kth;
+    }
+    if (lane == 0 && kth) atomicMax(&thr, kth);
+    __syncthreads();
+    if (threadIdx.x < G && G >= k && first[threadIdx.x]) {  // the k-th best list maximum
+        const unsigned long long me = first[threadIdx.x];
+        int r = 0;
+        for (int c = 0; c < G; c++) r += first[c] > me;
+        if (r == k - 1) atomicMax(&thr, me);
+    }
+    __syncthreads();
+    const unsigned long long T = thr >> 14;
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+        const int pos = tk_append(key[u] && (key[u] >> 14) >= T, &nsurv);
+        if (pos >= 0 && pos < 4096) surv[pos] = key[u];
+    }
+    __syncthreads();
+    const int ns = min(nsurv, 4096);  // <= k * k
+    tk_rank(surv, ns, k, [&](int r, unsigned long long kk) {
+        const int j = (int)(kk & 0x3FFFu);
+        out_i[r] = cand_i[j];
+        out_v[r] = cand_v[j];
+    });
+    for (int r = ns + threadIdx.x; r < k; r += blockDim.x) {
+        out_i[r] = -1;
+        out_v[r] = 0.f;
+    }
 }
 
 // GQA decode attention with an explicit T (no step state); 7 query heads

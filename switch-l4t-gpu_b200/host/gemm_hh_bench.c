@@ -101,7 +101,11 @@ int main(int argc, char **argv) {
     const double bytes = (double)wbytes + (double)B * K * 2 + (double)B * N * 4;
     printf("{\"N\": %d, \"K\": %d, \"B\": %d, \"path\": \"%s\", \"us\": %.3f, \"GB_s\": %.1f, \"bytes\": %.0f, "
            "\"copies\": %ld, \"max_rel\": %.3g, \"device_error\": %d}\n",
-           N, K, B, cuda_core ? "gemv_hh (CUDA cores)" : "gemm_hh_tc (tcgen05)", us, bytes / (us * 1e-6) / 1e9,
+           N, K, B,
+           cuda_core ? "gemv_hh (CUDA cores)"
+           : (B <= 16 && N < 128L * sb_sm_count()) ? "gemm_hh_mma (mma.sync, one launch)"
+                                                    : "gemm_hh_tc (tcgen05)",
+           us, bytes / (us * 1e-6) / 1e9,
            bytes, copies, max_rel, err);
     return (max_rel <= 1e-4 && !err) ? 0 : 1;
 }

@@ -443,7 +443,7 @@ int sb_topk_penalized(const float *logits, int V, const int *ctx, int ctx_len, f
     SB_ARG(logits && V > 0 && ctx_len >= 0 && (ctx || ctx_len == 0) && idx_out && val_out, "bad top-k arguments");
     SB_ARG(top_k >= 1 && top_k <= 64 && temperature > 0.0f && rep_penalty > 0.0f, "bad top-k settings");
     const long G = CEIL_DIV(V, 1024);
-    SB_ARG(G * top_k <= 16384, "ceil(V / 1024) x top_k exceeds 16384 candidates");
+    SB_ARG(G * top_k <= 16384 && V <= (1 << 18), "V > 2^18, or ceil(V / 1024) x top_k exceeds 16384 candidates");
     sb_ctx *c = sb_ctx_get();
     if (!c) return SB_ERR_STATE;
     CUdeviceptr ws;
