@@ -243,6 +243,33 @@ extern "C" __global__ void __launch_bounds__(tck::THREADS, 1)
     }
 }
 
+// The same with four outputs per thread and the loads of up to 8 splits
+// issued before the adds (the one-float loop was latency-bound: ~5 us for
+// the prefill's 14-22-way splits of 62 x 896).  total % 4 == 0, 16-byte
+// aligned ws and Y.
+extern "C" __global__ void gemm_splitk_reduce4(const float *__restrict__ ws, float *__restrict__ Y, long total,
+                                               int splits) {
+    const long n4 = total / 4;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < splits; s0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                v[j] = s0 + j < splits ? __ldcg(reinterpret_cast<const float4 *>(ws + (size_t)(s0 + j) * total) + i)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (s0 + j < splits) {
+                    acc.x += v[j].x;
+                    acc.y += v[j].y;
+                    acc.z += v[j].z;
+                    acc.w += v[j].w;
+                }
+        }
+        reinterpret_cast<float4 *>(Y)[i] = acc;
+    }
+}
 // Y[b][n] = sum over splits s (in order) of ws[s][b][n].
 extern "C" __global__ void gemm_splitk_reduce(const float *__restrict__ ws, float *__restrict__ Y, long total,
                                               int splits) {

@@ -24,6 +24,7 @@ typedef enum {
     F_GEMM_HH_MMA8_W4,
     F_GEMM_HH_MMA16_W4,
     F_TOPK_PARTIAL,
+    F_SPLITK_REDUCE4,
     F_TOPK_MERGE,
     F_SGEMM_NAIVE,
     F_MEMBW,

@@ -24,6 +24,15 @@ static int ws_reserve(sb_ctx *c, size_t need, CUdeviceptr *ws) {
     return 0;
 }
 
+/* Y = the split-K partials ws[splits][total] added in split order */
+static int splitk_reduce(sb_ctx *c, CUdeviceptr ws, CUdeviceptr y, long total, int splits, void *stream) {
+    void *rargs[] = {&ws, &y, &total, &splits};
+    const int v4 = total % 4 == 0 && (y & 15) == 0 && (ws & 15) == 0;
+    long g = CEIL_DIV(v4 ? total / 4 : total, 256);
+    if (g > 8L * c->sms) g = 8L * c->sms;
+    return sb_launch(c, v4 ? F_SPLITK_REDUCE4 : F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
+}
+
 /* ------------------------------------------------------------------ SGEMM */
 int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K, int row0, int row1,
                   void *stream) {
@@ -287,10 +296,7 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
     rc = sb_launch(c, F_GEMM_HH_TC, (unsigned)(tiles * splits), 1, 192, smem, (CUstream)stream, args, 0);
     if (rc || splits == 1) return rc;
     long total = (long)B * N;
-    void *rargs[] = {&ws, &y, &total, &splits};
-    long g = CEIL_DIV(total, 256);
-    if (g > 8L * c->sms) g = 8L * c->sms;
-    return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
+    return splitk_reduce(c, ws, y, total, splits, stream);
 }
 
 /* rows x K fp32, K-major, box {32 k, 128 rows}, 128-byte swizzle */
@@ -369,10 +375,7 @@ static int sgemm3x_launch(sb_ctx *c, const float *A, const float *Bt, float *C, 
     rc = sb_launch(c, F_SGEMM_3XTF32, (unsigned)(tiles * splits), 1, 192, smem, (CUstream)stream, args, 0);
     if (rc || splits == 1) return rc;
     long total = (long)M * N;
-    void *rargs[] = {&ws, &cc, &total, &splits};
-    long g = CEIL_DIV(total, 256);
-    if (g > 8L * c->sms) g = 8L * c->sms;
-    return sb_launch(c, F_SPLITK_REDUCE, (unsigned)g, 1, 256, 0, (CUstream)stream, rargs, 0);
+    return splitk_reduce(c, ws, cc, total, splits, stream);
 }
 
 int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream) {

@@ -85,6 +85,7 @@ static const struct {
     [F_FP16_FLUSH] = {M_QWEN, "fp16_flush_subnormals"},
     [F_GEMM_HH_TC] = {M_TC, "gemm_hh_tc"},
     [F_SPLITK_REDUCE] = {M_TC, "gemm_splitk_reduce"},
+    [F_SPLITK_REDUCE4] = {M_TC, "gemm_splitk_reduce4"},
     [F_SGEMM_3XTF32] = {M_TC, "sgemm_3xtf32_tc"},
     [F_TRANSPOSE_F32] = {M_TC, "transpose_f32"},
     [F_PF_EMBED] = {M_QWEN, "qwen_pf_embed"},
