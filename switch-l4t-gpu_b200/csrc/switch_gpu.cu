@@ -245,29 +245,11 @@ extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_entry(A, B, C, M, N, K);
 }
 
-// Split-K form for products with fewer 128 x 128 tiles than the GPU has CTA
-// slots (e.g. 1024^3: 64 tiles on 148 SMs): CTA (tile, split) multiplies the
-// tile over k range split and writes it to ws[split][M][N]; the splits are
-// then added in split order (gemm_splitk_reduce), so results are
-// deterministic.  Needs M, N % 128 == 0, K % (16 * splits) == 0 and 16-byte
-// aligned pointers (the host checks).  grid = tiles * splits, block 256.
-extern "C" __global__ void __launch_bounds__(256, 2)
-    sgemm_b200_sk(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ ws, int M, int N, int K,
-                  int splits) {
-    if (blockDim.x * blockDim.y * blockDim.z != SG_THREADS) return;
-    __shared__ __align__(16) SgSmem s;
-    const int tiles = (M / SG_BM) * (N / SG_BN);
-    const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
-    if (tile >= tiles) return;
-    const int klen = K / splits;
-    sgemm_tiles<false>(A, B, ws + (size_t)split * M * N, M, N, K, threadIdx.x, tile, tiles, s, split * klen, klen);
-}
-
 // Stream-K form for products with fewer 128 x 128 tiles than two per SM
 // (1024^3: 64 tiles): the tiles x K/16 k-chunks of the product are cut into
 // gridDim.x equal contiguous ranges, one per CTA (two per SM), so every SM
-// gets the same work -- split-K over 4 left 40 of 148 SMs with one CTA
-// and the rest with two.  A range covers at most two tiles (it is shorter
+// gets the same work -- a split-K form (4 k-ranges per tile, partials added
+// by a second kernel) left 40 of 148 SMs with one CTA and the rest with two.  A range covers at most two tiles (it is shorter
 // than one tile's K); each piece goes to ws[2 * cta + piece] (a compact
 // 128 x 128 tile), and sgemm_stk_fixup adds a tile's pieces in CTA order
 // (deterministic) into C.
