@@ -71,9 +71,14 @@ int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K,
 
 /* The same CUDA-core SGEMM with its operand tiles staged by TMA
  * (cp.async.bulk.tensor into a 4-stage shared-memory ring, persistent CTAs,
- * a producer warp and eight compute warps): bit-identical to sb_sgemm (each
- * output one fma chain over k in order).  K % 4 == 0, N % 4 == 0, 16-byte
- * aligned pointers; any M, N.  No counterpart in the reference. */
+ * a producer warp and eight compute warps): bit-identical to a one-CTA-
+ * per-tile launch of sb_sgemm's kernel (each output one fma chain over k in
+ * order).  With fewer 128 x 128 tiles than SMs (M, N % 128 == 0, K % 32 ==
+ * 0) it runs stream-K -- each tile's k-slices split over CTAs, the pieces
+ * added in CTA order through the context's workspace (deterministic, not
+ * bit-identical to the single chain); sb_sgemm / sb_sgemm_rows take this
+ * path for such products.  K % 4 == 0, N % 4 == 0, 16-byte aligned
+ * pointers; any M, N.  No counterpart in the reference. */
 int sb_sgemm_tma(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
 
 /* ---- multi-GPU SGEMM (row panels + NCCL all-gather of C), one rank per GPU.

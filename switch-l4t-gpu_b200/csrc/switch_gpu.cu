@@ -277,10 +277,11 @@ extern "C" __global__ void __launch_bounds__(256, 2)
 // C tile t = the sum, in CTA order, of its pieces in ws.  One float4 of the
 // tile per thread, the loads of up to 8 pieces issued before the adds (a
 // loop of dependent piece loads ran at 1.4 TB/s from L2).  grid: tiles x
-// 16; block 256; G = sgemm_b200_stk's grid.
+// 16; block 256; G = the stream-K kernel's grid, bk its k-slice depth (16
+// for sgemm_b200_stk, 32 for sgemm_tma).
 extern "C" __global__ void __launch_bounds__(256) sgemm_stk_fixup(const float *__restrict__ ws, float *__restrict__ C,
-                                                                  int M, int N, int K, int G) {
-    const int tiles_n = N / SG_BN, tiles = (M / SG_BM) * tiles_n, nk = K / SG_BK;
+                                                                  int M, int N, int K, int G, int bk) {
+    const int tiles_n = N / SG_BN, tiles = (M / SG_BM) * tiles_n, nk = K / bk;
     const int t = blockIdx.x / 16, i = (blockIdx.x % 16) * 256 + threadIdx.x;  // float4 index in the tile
     if (t >= tiles) return;
     const long units = (long)tiles * nk, ub = (long)t * nk, ue = ub + nk;

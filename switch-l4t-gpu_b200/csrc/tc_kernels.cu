@@ -549,10 +549,12 @@ SB_DEV void mbar_arrive(uint64_t *mb) {
 }
 }  // namespace sgt
 
-// grid: min(tiles, SMs) CTAs; block sgt::THREADS; dynamic smem 1024 + STAGES * STAGE + 128.
+// grid: min(tiles, SMs) CTAs, or in stream-K mode (ws != null; M, N % 128 ==
+// 0, K % 32 == 0) G > tiles CTAs; block sgt::THREADS; dynamic smem 1024 +
+// STAGES * STAGE + 128.
 extern "C" __global__ void __launch_bounds__(sgt::THREADS, 1)
     sgemm_tma(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, float *__restrict__ C,
-              int M, int N, int K) {
+              int M, int N, int K, float *__restrict__ ws) {
     using namespace sgt;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -560,6 +562,29 @@ extern "C" __global__ void __launch_bounds__(sgt::THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN, ntiles = tiles_m * tiles_n;
     const int nk = (K + BK - 1) / BK;
+    // work items: whole tiles (ws == nullptr), or stream-K pieces -- the
+    // tiles x nk k-slices cut into gridDim.x equal ranges, one per CTA; a
+    // piece (one tile's slices within the range) goes to ws[2 * cta +
+    // piece] as a compact 128 x 128 tile for sgemm_stk_fixup to add up
+    const bool stk = ws != nullptr;
+    const long units = (long)ntiles * nk, u_end = units * (blockIdx.x + 1) / gridDim.x;
+    struct Item {
+        int tile, k0, k1;
+    };
+    auto next_item = [&](int item, long &u, Item &it) -> bool {
+        if (!stk) {
+            it.tile = blockIdx.x + item * gridDim.x;
+            it.k0 = 0;
+            it.k1 = nk;
+            return it.tile < ntiles;
+        }
+        if (u >= u_end) return false;
+        it.tile = (int)(u / nk);
+        it.k0 = (int)(u % nk);
+        it.k1 = (int)min((long)nk, u_end - (long)it.tile * nk);
+        u = (long)it.tile * nk + it.k1;
+        return true;
+    };
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             tck::mbar_init(&full[s], 1);
@@ -576,12 +601,13 @@ extern "C" __global__ void __launch_bounds__(sgt::THREADS, 1)
     };
     if (warp == 8) {
         if (lane == 0) {  // ---- TMA producer
-            long it = 0;
+            long it = 0, u = units * blockIdx.x / gridDim.x;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-                const int2 mn = tile_mn(tile);
+            Item w;
+            for (int item = 0; ok && next_item(item, u, w); item++) {
+                const int2 mn = tile_mn(w.tile);
                 const int m0 = mn.x, n0 = mn.y;
-                for (int kt = 0; kt < nk; kt++, it++) {
+                for (int kt = w.k0; kt < w.k1; kt++, it++) {
                     const int s = (int)(it % STAGES);
                     if (it >= STAGES && !(ok = tck::mbar_wait(&empty[s], (unsigned)(((it / STAGES) - 1) & 1)))) break;
                     unsigned char *st = smem + (size_t)s * STAGE;
@@ -599,17 +625,18 @@ extern "C" __global__ void __launch_bounds__(sgt::THREADS, 1)
     // ---- warps 0-7: compute
     const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15
     const int tx = (warp & 1) * 8 + (lane & 7);    // 0..15
-    long it = 0;
+    long it = 0, u = units * blockIdx.x / gridDim.x;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const int2 mn = tile_mn(tile);
+    Item w;
+    for (int item = 0; ok && next_item(item, u, w); item++) {
+        const int2 mn = tile_mn(w.tile);
         const int m0 = mn.x, n0 = mn.y;
         unsigned long long acc[8][4];
 #pragma unroll
         for (int i = 0; i < 8; i++)
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[i][j] = 0ull;
-        for (int kt = 0; kt < nk; kt++, it++) {
+        for (int kt = w.k0; kt < w.k1; kt++, it++) {
             const int s = (int)(it % STAGES);
             if (!(ok = tck::mbar_wait(&full[s], (unsigned)((it / STAGES) & 1)))) break;
             const float *As = reinterpret_cast<const float *>(smem + (size_t)s * STAGE);
@@ -642,6 +669,19 @@ extern "C" __global__ void __launch_bounds__(sgt::THREADS, 1)
             if (lane == 0) sgt::mbar_arrive(&empty[s]);  // this warp is done with the stage
         }
         if (!ok) break;
+        if (stk) {  // the piece, compact, to its workspace slot
+            float *pw = ws + (size_t)(2 * blockIdx.x + item) * BM * BN;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int hb = 0; hb < 2; hb++) {
+                    float4 o;
+                    f2_unpack(acc[i][hb * 2], o.x, o.y);
+                    f2_unpack(acc[i][hb * 2 + 1], o.z, o.w);
+                    *reinterpret_cast<float4 *>(pw + (ty + 16 * i) * BN + hb * 64 + tx * 4) = o;
+                }
+            continue;
+        }
         // epilogue: rows ty + 16 i, columns tx * 4 and 64 + tx * 4 (4 each)
 #pragma unroll
         for (int i = 0; i < 8; i++) {

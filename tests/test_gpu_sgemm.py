@@ -189,13 +189,17 @@ def test_split_k_small_products(cuda_dev, M, N, K, row0, row1):
     assert np.all(C[:row0] == 3.0) and np.all(C[row1:] == 3.0)  # rows outside the panel untouched
 
 
-@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (4096, 4096, 4096), (1000, 384, 1004), (129, 260, 36),
-                                   (128, 128, 32), (3, 4, 4)])
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (1000, 384, 1004), (129, 260, 36), (3, 4, 4),
+                                   (1024, 1024, 1024), (128, 128, 32), (1152, 1152, 512)])
 def test_sgemm_tma_bit_identical(cuda_dev, swmod, M, N, K):
     """The TMA-staged SGEMM gives the same bits as the register-staged kernel
     sgemm_b200 launched one CTA per tile (every output one fma chain over k
     in order) and meets the FP32 bar against the harness loop on sampled
-    rows, ragged shapes included (TMA zero-fills outside the matrices)."""
+    rows, ragged shapes included (TMA zero-fills outside the matrices).
+    Products with fewer tiles than SMs (M, N % 128 == 0, K % 32 == 0) run
+    stream-K -- each tile's k-slices split over CTAs, pieces added in CTA
+    order -- so there the bar is the FP32 one on every row, and two calls
+    give the same bits."""
     import torch
     A, B = _mats(M, N, K, 31)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
@@ -206,7 +210,15 @@ def test_sgemm_tma_bit_identical(cuda_dev, swmod, M, N, K):
     sb200.sgemm_tma(dA, dB, got, M, N, K)
     torch.cuda.synchronize()
     assert sb200.tc_error() == 0
-    assert torch.equal(got, want)
     C = got.cpu().numpy()
-    for r in sorted({0, M // 2, M - 1}):
-        assert _rel_frob(C[r], orc.sgemm(A, B, r, r + 1)[r]) <= REL_FROB
+    stream_k = tiles < sb200.sm_count() and M % 128 == 0 and N % 128 == 0 and K % 32 == 0
+    if not stream_k:
+        assert torch.equal(got, want)
+        for r in sorted({0, M // 2, M - 1}):
+            assert _rel_frob(C[r], orc.sgemm(A, B, r, r + 1)[r]) <= REL_FROB
+    else:
+        assert _rel_frob(C, orc.sgemm(A, B)) <= REL_FROB
+        again = torch.full((M, N), float("nan"), device="cuda")
+        sb200.sgemm_tma(dA, dB, again, M, N, K)
+        torch.cuda.synchronize()
+        assert torch.equal(got, again)
