@@ -21,9 +21,10 @@ scaling "weak".  The weights (988 MB) exceed the 126 MB L2, so no flush is
 needed between timed steps.
 
 Secondary keys of the same line: "sgemm" -- 16384^3 FP32 SGEMM sharded by
-row panels over all ranks (strong scaling) with the NCCL all-gather of C,
-compute-only and with the gather, per-GPU fraction of the live FP32 FMA
-peak; "sgemm_3xtf32" -- the same on the opt-in 3xTF32 tensor-core kernel;
+row panels over all ranks (strong scaling), C gathered on every rank by the
+kernel's own stores into the peers' C over NVLink (the NCCL all-gather of C
+timed beside it), compute-only and with the gather, per-GPU fraction of the
+live FP32 FMA peak; "sgemm_3xtf32" -- the same on the opt-in 3xTF32 tensor-core kernel;
 "gemv" -- the standalone FP16 GEMV sweep (batch 1 on CUDA cores, 4 and 16
 on the tcgen05 tensor cores) in GB/s against the HBM peak; "gpt2_decode" --
 configs[1], GPT-2-124M-shape FP32 decode (16 prompt tokens, 128 new), with
@@ -349,7 +350,10 @@ def sgemm_section(torch, dev, dist_on, steps, warmup, kernel="fp32"):
     """16384^3 FP32 SGEMM row-panel sharded over all ranks (strong scaling):
     compute-only and with the NCCL all-gather of C, max over ranks; at N > 1
     also the chunked form (4 row chunks, each gathered while the next is
-    multiplied) and a check of the gathered C on every rank.
+    multiplied) and, for the FP32 kernel, the fused form (the kernel stores
+    every tile into every rank's C over NVLink: PanelSgemm gather_mode
+    "peer"), which is then the reported path; the C every rank holds is
+    checked on every rank.
     kernel "3xtf32" is the opt-in tensor-pipe variant (reported separately)."""
     import sgemm_dist
     n = SGEMM_N
@@ -403,24 +407,48 @@ def sgemm_section(torch, dev, dist_on, steps, warmup, kernel="fp32"):
         ov = e0.elapsed_time(e1)
         del pc
         torch.cuda.empty_cache()
-    t = torch.tensor([comp, tot, ov], dtype=torch.float64, device=dev)
+    peer_ms, pp = 0.0, None
+    if ps.world > 1 and kernel == "fp32":  # fused: every tile stored into every rank's C by the kernel
+        pp = sgemm_dist.PanelSgemm(n, n, n, gather_mode="peer")
+        for _ in range(max(1, warmup)):
+            pp(A, B)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for _ in range(steps):
+            pp(A, B)
+        e1.record(cur)
+        torch.cuda.synchronize()
+        peer_ms = e0.elapsed_time(e1)
+    t = torch.tensor([comp, tot, ov, peer_ms], dtype=torch.float64, device=dev)
     if dist_on:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    comp_ms, tot_ms, ov_ms = float(t[0]) / steps, float(t[1]) / steps, float(t[2]) / steps
+    comp_ms, tot_ms, ov_ms, peer_ms = (float(v) / steps for v in t)
     # the result every rank holds after the gather, checked on every rank
-    ps(A, B)
+    # (the fused form's C when it ran: it is the reported path)
+    if pp is not None:
+        pp(A, B)
+    else:
+        ps(A, B)
     torch.cuda.synchronize()
-    fr, rel, bad = gathered_c_check(torch, dev, ps, B, n, dist_on)
+    fr, rel, bad = gathered_c_check(torch, dev, pp if pp is not None else ps, B, n, dist_on)
+    if pp is not None:
+        pp.close()
+        del pp
     verdict = "CORRECT" if fr <= 1e-5 and rel <= 1e-5 and bad == 0 else "WRONG"
     flop = 2.0 * n ** 3
     per_gpu = 2.0 * ps.rows * n * n / (comp_ms * 1e-3) / 1e12
+    step_ms = peer_ms if peer_ms else tot_ms
     res = {"n": n, "n_gpus": WORLD, "kernel": "sgemm_b200" if kernel == "fp32" else "sgemm_3xtf32_tc",
-           "value": round(flop / (tot_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "value": round(flop / (step_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "gather": ("tiles stored into every rank's C by the kernel (NVLink peer stores)" if peer_ms
+                      else "NCCL all-gather" if WORLD > 1 else "none (1 GPU)"),
            "compute_tflops": round(flop / (comp_ms * 1e-3) / 1e12, 2), "compute_ms": round(comp_ms, 3),
-           "allgather_ms": round(tot_ms - comp_ms, 3), "ms_per_step": round(tot_ms, 3)}
+           "ms_per_step": round(step_ms, 3), "allgather_ms": round(tot_ms - comp_ms, 3)}
+    if peer_ms:
+        res["nccl_ms"] = round(tot_ms, 3)  # the panel, then the NCCL all-gather
     if ov_ms:
         res["chunked4_ms"] = round(ov_ms, 3)
-        res["chunked4_tflops"] = round(flop / (ov_ms * 1e-3) / 1e12, 2)
     res.update({"check": {"verdict": verdict, "freivalds": float("%.2e" % fr), "rows_rel": float("%.2e" % rel),
                           "bad_cells": bad},
                 "roofline": {"bound": bound, "achieved_per_gpu": round(per_gpu, 2), "peak": round(peak, 2),
@@ -825,9 +853,10 @@ def run_b200(args):
     if not args.no_secondary:
         # the strong-scaling SGEMM rows of configs[4] close the line, so a
         # reader that keeps only its tail still has them at every N
-        line["sgemm_note"] = ("configs[4]: 16384^3 FP32 row panels over n_gpus ranks, B replicated, NCCL "
-                              "all-gather of C; value includes the gather; per-GPU roofline vs the live FMA peak; "
-                              "gathered C checked on every rank (FP64 Freivalds + exact rows)")
+        line["sgemm_note"] = ("configs[4]: 16384^3 FP32 row panels over n_gpus ranks, B replicated; C gathered "
+                              "by peer stores from the FP32 kernel (nccl_ms: panel + NCCL all-gather); value "
+                              "includes the gather; per-GPU roofline vs the live FMA peak; gathered C checked on "
+                              "every rank (FP64 Freivalds + exact rows)")
         line["sgemm"] = sg
         line["sgemm_3xtf32"] = sg3
     if RANK == 0:

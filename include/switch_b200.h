@@ -81,6 +81,31 @@ int sb_sgemm_rows(const float *A, const float *B, float *C, int M, int N, int K,
  * pointers; any M, N.  No counterpart in the reference. */
 int sb_sgemm_tma(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
 
+/* C[d] = A . B for d < nc (nc <= SB_SGEMM_MAX_DST): every finished 128 x 128
+ * tile is stored into each output -- this device's memory or a peer's,
+ * mapped into this process (sb_ipc_open or peer access) -- by the kernel
+ * that computed it, so a row-panel product lands in every rank's C over
+ * NVLink while the other tiles are still being multiplied, with no
+ * separate all-gather.  Plain stores (no TMA); the kernel ends with a
+ * system-scope fence, and the caller orders the peers' readers after it (a
+ * collective or an event on their streams).  M, N % 128 == 0, K % 16 == 0,
+ * 16-byte aligned pointers.  The same arithmetic as sb_sgemm's one-CTA-per-
+ * tile kernel: every output one fma chain over k in order.  No counterpart
+ * in the reference, which has no multi-GPU path. */
+#define SB_SGEMM_MAX_DST 8
+int sb_sgemm_multi(const float *A, const float *B, float *const *C, int nc, int M, int N, int K, void *stream);
+
+/* Device memory shared with the other processes of one node (CUDA IPC):
+ * sb_ipc_export writes the 64-byte handle of the allocation that holds
+ * `ptr` and ptr's offset in it; sb_ipc_open maps a handle another process
+ * exported into this process's current context and returns its base +
+ * offset; sb_ipc_close unmaps it (pass the pointer and offset sb_ipc_open
+ * took).  The exporting process must keep the memory allocated until every
+ * importer has closed it.  No counterpart in the reference. */
+int sb_ipc_export(const void *ptr, void *handle64, size_t *offset);
+int sb_ipc_open(const void *handle64, size_t offset, void **ptr);
+int sb_ipc_close(void *ptr, size_t offset);
+
 /* ---- multi-GPU SGEMM (row panels + NCCL all-gather of C), one rank per GPU.
  * No counterpart in the reference, which runs on device 0 only
  * (gpu_workload.c:66-67).  NCCL is loaded at run time (libnccl.so.2).

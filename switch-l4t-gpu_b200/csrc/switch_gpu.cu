@@ -44,6 +44,15 @@ struct SgSmem {
     float As[2][SG_BK][SG_BM];  // k-major, 16-byte units swizzled by sg_swz(k)
     float Bs[2][SG_BK][SG_BN];
 };
+// Output matrices of the multi-destination form (sgemm_b200_dst): every
+// finished tile is stored into each of them -- this GPU's C and the C of
+// each peer rank, mapped into this process -- so the row panels of all
+// ranks meet in every rank's C with no separate all-gather.
+#define SG_MAX_DST 8
+struct SgDst {
+    float *c[SG_MAX_DST];
+    int n;
+};
 __device__ __forceinline__ int sg_swz(int k) { return (k >> 2) << 2; }
 
 // One k-slice into registers with zero fill outside the matrices: A row
@@ -74,14 +83,39 @@ __device__ __forceinline__ void sg_store_slice(SgSmem &s, int buf, int ams, int 
     *reinterpret_cast<float4 *>(&s.Bs[buf][br][bc]) = rb;
 }
 
+// 64 rows x 128 columns staged in shared memory -> rows r0.., columns n0..
+// of C (or of every destination): each warp stores whole 512-byte row
+// segments.  Not inlined, so the stores' registers never weigh on the main
+// loop's.  (With the 8 x 8 register tile written straight from the
+// registers, the kernel kept more spills in its loop and took 3 % longer
+// at 8192 x 16384 x 16384.)
+__device__ __noinline__ void sg_copy_out1(const float *st, float *C, int r0, int n0, int N, int tid) {
+    for (int k = tid; k < 64 * SG_BN / 4; k += SG_THREADS) {
+        const int row = k / (SG_BN / 4), c4 = k % (SG_BN / 4);
+        *reinterpret_cast<float4 *>(C + (size_t)(r0 + row) * N + n0 + c4 * 4) =
+            *reinterpret_cast<const float4 *>(st + row * SG_BN + c4 * 4);
+    }
+}
+__device__ __noinline__ void sg_copy_out(const float *st, const SgDst *dst, int r0, int n0, int N, int tid) {
+    for (int k = tid; k < 64 * SG_BN / 4; k += SG_THREADS) {
+        const int row = k / (SG_BN / 4), c4 = k % (SG_BN / 4);
+        const float4 v = *reinterpret_cast<const float4 *>(st + row * SG_BN + c4 * 4);
+        const size_t off = (size_t)(r0 + row) * N + n0 + c4 * 4;
+        for (int d = 0; d < dst->n; d++) *reinterpret_cast<float4 *>(dst->c[d] + off) = v;
+    }
+}
+
 // k range [kbeg, kbeg + klen) of the product (split-K: the unpredicated
 // path only, kbeg and klen multiples of SG_BK); K stays A's row stride.
 // LOCAL: the tile is written to C as a compact 128 x 128 block (a piece of
 // a tile in the stream-K form) instead of at its place in the M x N matrix.
-template <bool EDGE, bool LOCAL = false>
+// MULTI (unpredicated path only): the tile goes to every matrix of *dst
+// instead of C.
+template <bool EDGE, bool LOCAL = false, bool MULTI = false>
 __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const float *__restrict__ B,
                                             float *__restrict__ C, int M, int N, int K, int tid, int cta,
-                                            int ncta, SgSmem &s, int kbeg = 0, int klen = -1) {
+                                            int ncta, SgSmem &s, int kbeg = 0, int klen = -1,
+                                            const SgDst *dst = nullptr) {
     if (klen < 0) klen = K;
     const int warp = tid >> 5, lane = tid & 31;
     const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15
@@ -163,7 +197,28 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
             }
             __syncthreads();
         }
-        // epilogue
+        if (!EDGE && !LOCAL) {
+            // whole tiles: through shared memory, 64 rows at a time, stored
+            // as whole 512-byte row segments to C (or every destination)
+            float *st = reinterpret_cast<float *>(&s);  // 8192 floats: one half-tile
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int hb = 0; hb < 2; hb++) {
+                        float4 o;
+                        f2_unpack(acc[4 * h + i][hb * 2], o.x, o.y);
+                        f2_unpack(acc[4 * h + i][hb * 2 + 1], o.z, o.w);
+                        *reinterpret_cast<float4 *>(st + (ty * 4 + i) * SG_BN + hb * 64 + tx * 4) = o;
+                    }
+                __syncthreads();
+                if (MULTI) sg_copy_out(st, dst, m0 + 64 * h, n0, N, tid);
+                else sg_copy_out1(st, C, m0 + 64 * h, n0, N, tid);
+                __syncthreads();  // the half is read before the next one (or the next tile) overwrites it
+            }
+        } else {
+        // epilogue of partial tiles and stream-K pieces: straight from the registers
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int r = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
@@ -183,6 +238,7 @@ __device__ __forceinline__ void sgemm_tiles(const float *__restrict__ A, const f
                     if (c + 3 < N) p[3] = o.w;
                 }
             }
+        }
         }
     }
 }
@@ -243,6 +299,22 @@ extern "C" __global__ void __launch_bounds__(256, 2)
 extern "C" __global__ void __launch_bounds__(256, 2)
     sgemm_b200(const float *__restrict__ A, const float *__restrict__ B, float *__restrict__ C, int M, int N, int K) {
     sgemm_entry(A, B, C, M, N, K);
+}
+
+// The multi-destination form: C = A.B for whole tiles (M, N % 128 == 0,
+// K % 16 == 0, 16-byte aligned), each tile stored into every matrix of
+// dst -- up to SG_MAX_DST, local or peer-mapped over NVLink (plain stores,
+// no TMA).  The system-scope fence at the end makes this CTA's remote
+// stores visible to the peers before the kernel completes; the caller
+// orders their readers after the kernel (a collective, an event).
+// One CTA per tile, block 256.
+extern "C" __global__ void __launch_bounds__(256, 2)
+    sgemm_b200_dst(const float *__restrict__ A, const float *__restrict__ B, const __grid_constant__ SgDst dst,
+                   int M, int N, int K) {
+    if (blockDim.x * blockDim.y * blockDim.z != SG_THREADS) return;
+    __shared__ __align__(16) SgSmem s;
+    sgemm_tiles<false, false, true>(A, B, nullptr, M, N, K, threadIdx.x, blockIdx.x, gridDim.x, s, 0, -1, &dst);
+    __threadfence_system();
 }
 
 // Stream-K form for products with fewer 128 x 128 tiles than two per SM

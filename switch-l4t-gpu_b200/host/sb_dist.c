@@ -199,3 +199,35 @@ int sb_nccl_wait(void *comm, void *stream, double timeout_s) {
         nanosleep(&ts, NULL);
     }
 }
+
+/* ---- CUDA IPC: the C of every rank mapped into every other rank's process,
+ * so sb_sgemm_multi can store a panel's tiles straight into all of them. */
+int sb_ipc_export(const void *ptr, void *handle64, size_t *offset) {
+    SB_ARG(ptr && handle64 && offset, "bad ipc export arguments");
+    if (!sb_ctx_get()) return SB_ERR_STATE;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    SB_CK(cuMemGetAddressRange(&base, &size, (CUdeviceptr)(uintptr_t)ptr));
+    CUipcMemHandle h;
+    SB_CK(cuIpcGetMemHandle(&h, base));
+    memcpy(handle64, &h, sizeof h);
+    *offset = (size_t)((CUdeviceptr)(uintptr_t)ptr - base);
+    return 0;
+}
+
+int sb_ipc_open(const void *handle64, size_t offset, void **ptr) {
+    SB_ARG(handle64 && ptr, "bad ipc open arguments");
+    if (!sb_ctx_get()) return SB_ERR_STATE;
+    CUipcMemHandle h;
+    memcpy(&h, handle64, sizeof h);
+    CUdeviceptr base = 0;
+    SB_CK(cuIpcOpenMemHandle(&base, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS));
+    *ptr = (void *)(uintptr_t)(base + offset);
+    return 0;
+}
+
+int sb_ipc_close(void *ptr, size_t offset) {
+    SB_ARG(ptr, "bad ipc close arguments");
+    SB_CK(cuIpcCloseMemHandle((CUdeviceptr)(uintptr_t)ptr - offset));
+    return 0;
+}

@@ -15,6 +15,7 @@ enum { M_SWITCH = 0, M_GEMV, M_GPT2, M_QWEN, M_TC, M_COUNT };
 
 typedef enum {
     F_SGEMM_B200 = 0,
+    F_SGEMM_B200_DST,
     F_SGEMM_B200_STK,
     F_SGEMM_STK_FIXUP,
     F_SGEMM_TMA,

@@ -34,6 +34,7 @@ static const struct {
     const char *name;
 } fn_table[F_COUNT] = {
     [F_SGEMM_B200] = {M_SWITCH, "sgemm_b200"},
+    [F_SGEMM_B200_DST] = {M_SWITCH, "sgemm_b200_dst"},
     [F_SGEMM_B200_STK] = {M_SWITCH, "sgemm_b200_stk"},
     [F_SGEMM_STK_FIXUP] = {M_SWITCH, "sgemm_stk_fixup"},
     [F_SGEMM_TMA] = {M_TC, "sgemm_tma"},

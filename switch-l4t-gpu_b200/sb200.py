@@ -77,6 +77,10 @@ def lib():
     _sig(L.sb_sm_count, I)
     _sig(L.sb_sgemm, I, P, P, P, I, I, I, P)
     _sig(L.sb_sgemm_rows, I, P, P, P, I, I, I, I, I, P)
+    _sig(L.sb_sgemm_multi, I, P, P, ctypes.POINTER(P), I, I, I, I, P)
+    _sig(L.sb_ipc_export, I, P, P, ctypes.POINTER(ctypes.c_size_t))
+    _sig(L.sb_ipc_open, I, P, ctypes.c_size_t, ctypes.POINTER(P))
+    _sig(L.sb_ipc_close, I, P, ctypes.c_size_t)
     _sig(L.sb_membw_read4, I, P, P, I, I, I, P)
     _sig(L.sb_fma_peak, I, P, I, I, P, ctypes.POINTER(D))
     _sig(L.sb_gemv_f32, I, P, P, P, P, I, I, P)
@@ -186,6 +190,32 @@ def sgemm_tma(A, B, C, M, N, K, stream=None):
 
 def sgemm_rows(A, B, C, M, N, K, row0, row1, stream=None):
     check(lib().sb_sgemm_rows(_p(A), _p(B), _p(C), M, N, K, row0, row1, _s(stream)))
+
+
+def sgemm_multi(A, B, outs, M, N, K, stream=None):
+    """C = A.B stored into every matrix of `outs` (tensors or raw device
+    addresses, local or peer-mapped; at most 8): sb_sgemm_multi."""
+    arr = (ctypes.c_void_p * len(outs))(*[_p(c) for c in outs])
+    check(lib().sb_sgemm_multi(_p(A), _p(B), arr, len(outs), M, N, K, _s(stream)))
+
+
+def ipc_export(t):
+    """(64-byte CUDA IPC handle of the allocation holding `t`, t's offset in it)."""
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_size_t()
+    check(lib().sb_ipc_export(_p(t), h, ctypes.byref(off)))
+    return h.raw, off.value
+
+
+def ipc_open(handle, offset):
+    """Device address, in this process, of a buffer another process exported."""
+    p = ctypes.c_void_p()
+    check(lib().sb_ipc_open(ctypes.create_string_buffer(handle, 64), offset, ctypes.byref(p)))
+    return p.value
+
+
+def ipc_close(addr, offset):
+    check(lib().sb_ipc_close(addr, offset))
 
 
 def membw_read4(buf, out, n4, iters, grid=0, stream=None):

@@ -16,6 +16,13 @@ gpu_workload.c:88-90) -- split across P ranks, one process per GPU:
     chunk i+1 is multiplied (gather on a second stream, ordered by events);
     the chunk-major staging is permuted into C with one device copy at the
     end.
+  * gather_mode="peer" fuses the gather into the product: every rank maps
+    the other ranks' C into its process (CUDA IPC), and the kernel
+    (sb_sgemm_multi) stores each finished 128 x 128 tile into all of them
+    over NVLink while it multiplies the next -- no all-gather, no staging.
+    One-element collectives before and after order it: nobody still reads
+    the previous C when the stores start, and every rank's tiles have
+    landed when the call's stream moves on.
 
 The reference has no multi-GPU path; the sharding rule (row panels, B
 replicated, all-gather of C) is this package's own.  The compute hook exists
@@ -59,9 +66,13 @@ class PanelSgemm:
     B:       the whole B (K x N), replicated on every rank.
     kernel:  "fp32" (CUDA-core FFMA, the default) or "3xtf32" (opt-in, the
              TF32 tensor pipe with the 3xTF32 split).
+    gather_mode: "nccl" (the panel, then an NCCL all-gather) or "peer" (the
+             fp32 kernel stores every tile into every rank's C; needs M a
+             multiple of 128 x world, N of 128 and K of 16; call close()
+             on every rank before the buffers go away).
     """
 
-    def __init__(self, M, N, K, group=None, device=None, chunks=1, compute=None, kernel="fp32"):
+    def __init__(self, M, N, K, group=None, device=None, chunks=1, compute=None, kernel="fp32", gather_mode="nccl"):
         if M <= 0 or N <= 0 or K <= 0 or chunks < 1:
             raise ValueError("PanelSgemm: M, N, K and chunks must be positive")
         self.M, self.N, self.K = M, N, K
@@ -85,6 +96,45 @@ class PanelSgemm:
             self.mine = torch.empty(self.chunks, self.rc, N, dtype=torch.float32, device=self.device)
         self.is_cuda = self.device.type == "cuda"
         self.comm = torch.cuda.Stream(self.device) if self.is_cuda and self.chunks > 1 else None
+        if gather_mode not in ("nccl", "peer"):
+            raise ValueError("PanelSgemm: gather_mode must be 'nccl' or 'peer'")
+        self.gather_mode = gather_mode if self.world > 1 else "nccl"
+        self._peers = {}
+        if self.gather_mode == "peer":
+            if kernel != "fp32" or compute is not None or self.chunks != 1 or not self.is_cuda:
+                raise ValueError("PanelSgemm: peer gather runs the fp32 CUDA kernel, chunks=1")
+            if M % (128 * self.world) or N % 128 or K % 16:
+                raise ValueError("PanelSgemm: peer gather needs M % (128 x world) == 0, N % 128 == 0, K % 16 == 0")
+            self._open_peers()
+
+    def _open_peers(self):
+        import sb200
+        mine = sb200.ipc_export(self.C_pad)
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=self.group)
+        base = {}
+        for r in range(self.world):
+            if r == self.rank:
+                base[r] = self.C_pad.data_ptr()
+            else:
+                base[r] = sb200.ipc_open(*every[r])
+                self._peers[r] = (base[r], every[r][1])
+        # this rank's panel rows inside every rank's C; its own C first
+        off = self.row0 * self.N * 4
+        self._dsts = [base[self.rank] + off] + [base[r] + off for r in range(self.world) if r != self.rank]
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def close(self):
+        """Unmap the peers' C (peer gather; a collective: every rank calls it)."""
+        if self.gather_mode != "peer" or not self._peers:
+            return
+        import sb200
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still stores into a C
+        for addr, off in self._peers.values():
+            sb200.ipc_close(addr, off)
+        self._peers = {}
+        dist.barrier(group=self.group)  # every mapping is gone before an owner may free its C
 
     def panel(self):
         """This rank's panel of C (a view of the gathered buffer)."""
@@ -116,6 +166,17 @@ class PanelSgemm:
         if not gather or self.world == 1:
             self.multiply(A_panel, B, stream)
             return self.C if self.world == 1 else self.panel()
+        if self.gather_mode == "peer":
+            import sb200
+            if not self._peers:
+                raise RuntimeError("PanelSgemm: closed")
+            self._check(A_panel, B)
+            s = self._stream(stream)
+            with torch.cuda.stream(s):
+                dist.all_reduce(self._flag, op=dist.ReduceOp.MAX, group=self.group)  # the previous C is read
+                sb200.sgemm_multi(A_panel, B, self._dsts, self.rows, self.N, self.K, s)
+                dist.all_reduce(self._flag, op=dist.ReduceOp.MAX, group=self.group)  # every panel has landed
+            return self.C
         if self.chunks == 1:
             s = self._stream(stream)
             self.multiply(A_panel, B, s)

@@ -222,3 +222,31 @@ def test_sgemm_tma_bit_identical(cuda_dev, swmod, M, N, K):
         sb200.sgemm_tma(dA, dB, again, M, N, K)
         torch.cuda.synchronize()
         assert torch.equal(got, again)
+
+
+@pytest.mark.parametrize("M,N,K,nout", [(1024, 1024, 1024, 2), (256, 384, 48, 3), (128, 128, 16, 1)])
+def test_sgemm_multi_outputs_bit_identical(cuda_dev, swmod, M, N, K, nout):
+    """sb_sgemm_multi stores every tile into each output (here all on this
+    GPU): each equals the one-CTA-per-tile sgemm_b200 launch bit for bit and
+    meets the FP32 bar against the harness loop on sampled rows."""
+    import torch
+    A, B = _mats(M, N, K, 41)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    want = torch.zeros((M, N), device="cuda")
+    swmod.launch("sgemm_b200", ((M // 128) * (N // 128),), (256,), dA, dB, want, M, N, K)
+    outs = [torch.full((M, N), float("nan"), device="cuda") for _ in range(nout)]
+    sb200.sgemm_multi(dA, dB, outs, M, N, K)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, want)
+    C = outs[0].cpu().numpy()
+    for r in sorted({0, M // 2, M - 1}):
+        assert _rel_frob(C[r], orc.sgemm(A, B, r, r + 1)[r]) <= REL_FROB
+
+
+def test_sgemm_multi_rejects_partial_tiles(cuda_dev):
+    import torch
+    a = torch.zeros(256 * 64, device="cuda")
+    for (M, N, K, nout) in [(100, 128, 16, 1), (128, 100, 16, 1), (128, 128, 20, 1), (128, 128, 16, 9)]:
+        with pytest.raises(RuntimeError):
+            sb200.sgemm_multi(a, a, [a] * nout, M, N, K)

@@ -34,13 +34,43 @@ def test_single_rank_panel(cuda_dev, M, N, K):
     assert orc.freivalds(A, B, np.ascontiguousarray(C)) <= 1e-5
 
 
+def test_ipc_stores_from_another_process(cuda_dev):
+    """The peer-store path on one GPU: this process exports C (CUDA IPC), a
+    child process maps it and runs sb_sgemm_multi into its own buffer and
+    into this C.  Every cell arrives, bit-identical to this process's own
+    sgemm_b200 launch, within the FP32 bar of the harness loop.  (The two
+    processes' kernels never wait on each other.)"""
+    import torch
+    import drv
+    M, N, K, seed = 512, 384, 256, 77
+    A = sb200.synth_uniform(M * K, -1.0, 1.0, seed).reshape(M, K)
+    B = sb200.synth_uniform(K * N, -1.0, 1.0, seed + 1).reshape(K, N)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    C = torch.full((M, N), float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    handle, offset = sb200.ipc_export(C)
+    cmd = [sys.executable, os.path.join(HERE, "ipc_sgemm_worker.py"), handle.hex(), str(offset),
+           str(M), str(N), str(K), str(seed)]
+    r = subprocess.run(["timeout", "-k", "10", "120"] + cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    want = torch.zeros((M, N), device="cuda")
+    drv.Module(sb200.CUBINS["switch_gpu"]).launch("sgemm_b200", ((M // 128) * (N // 128),), (256,), dA, dB, want,
+                                                  M, N, K)
+    torch.cuda.synchronize()
+    assert torch.equal(C, want)
+    assert float(r.stdout.split()[-1]) == float(want.double().sum())
+    ref = orc.sgemm(A, B)
+    rows = [0, 255, 511]
+    assert np.linalg.norm(C.cpu().numpy()[rows] - ref[rows]) <= 1e-5 * np.linalg.norm(ref[rows])
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def test_two_ranks_nccl_allgather(cuda_dev):
+def test_two_ranks_nccl_allgather_and_peer_stores(cuda_dev):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -49,4 +79,5 @@ def test_two_ranks_nccl_allgather(cuda_dev):
            "--master-addr=127.0.0.1", f"--master-port={_free_port()}", os.path.join(HERE, "dist_sgemm_worker.py")]
     r = subprocess.run(["timeout", "-k", "30", "400"] + cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
-    assert r.stdout.count(" ok") == 6, r.stdout
+    import dist_sgemm_worker
+    assert r.stdout.count(" ok") == 2 * len(dist_sgemm_worker.CASES), r.stdout
