@@ -179,6 +179,15 @@ int sb_gemm_hh(const uint16_t *W, const uint16_t *X, float *Y, int K, int N, int
  * error ~1e-6) and tensor-core speed.  K % 4 == 0, N % 4 == 0, 16-byte
  * aligned pointers.  No counterpart in the reference. */
 int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int K, void *stream);
+/* The same product stored into every output C[d], d < nc <= SB_SGEMM_MAX_DST
+ * (local or peer-mapped, as sb_sgemm_multi): each finished row of a tile
+ * goes to all of them with plain stores, and the kernel ends with a
+ * system-scope fence.  M, N % 128 == 0, K % 4 == 0, 16-byte aligned
+ * pointers; no K split.  Bit-identical to sb_sgemm_3xtf32 whenever that
+ * call runs without a K split (128 x 128 tiles at least as many as SMs).
+ * No counterpart in the reference. */
+int sb_sgemm_3xtf32_multi(const float *A, const float *B, float *const *C, int nc, int M, int N, int K,
+                          void *stream);
 /* The same product with the second operand given transposed: C = A Bt^T for
  * Bt [N][K] row-major (an [out][in] weight matrix), no transpose pass.  Same
  * alignment rules.  No counterpart in the reference. */

@@ -338,15 +338,27 @@ SB_DEV void mbar_arrive(uint64_t *mb) {
 }
 }  // namespace t3
 
+// Outputs of the multi-destination form (sgemm_3xtf32_tc_dst): each
+// finished row of a tile is stored into every one of them -- this GPU's C
+// and the peer ranks' C mapped into this process -- so a row-panel product
+// reaches every rank with no separate all-gather.
+#define T3_MAX_DST 8
+struct T3Dst {
+    float *c[T3_MAX_DST];
+    int n;
+};
+
 // grid: ceil(M/128) * ceil(N/128) * splits CTAs (blockIdx.x = (tile_m *
 // tiles_n + tile_n) * splits + split); block t3::THREADS; dynamic smem:
 // 1024 + STAGES * STAGE + 256 bytes.  splits == 1: C; else ws[split][M][N].
-extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
-    sgemm_3xtf32_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_bt,
-                    float *__restrict__ C, int M, int N, int K, float *__restrict__ ws, int splits) {
+// MULTI (splits == 1, N % 128 == 0): every matrix of *dst instead of C.
+template <bool MULTI>
+__device__ __forceinline__ void sgemm3x_body(const CUtensorMap &tm_a, const CUtensorMap &tm_bt, float *__restrict__ C,
+                                             int M, int N, int K, float *__restrict__ ws, int splits,
+                                             const T3Dst *dst) {
     using namespace t3;
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) unsigned char smem_raw3[];  // the dynamic shared memory (one name per function)
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw3) + 1023) & ~uintptr_t(1023));
     // stage s: [A | Bt | A small | Bt small], 16 KB each
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE);
     uint64_t *full = bars, *conv = bars + STAGES, *empty = bars + 2 * STAGES;
@@ -479,7 +491,25 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
         }
         while (ok && promoted < nchunks) promote(promoted++);
         const int row = m0 + quarter * 32 + lane;
-        if (ok && row < M) {
+        if (MULTI) {
+            // this warp's 32 rows through the drained stage buffers (rows
+            // 132 floats apart: each float4 store of the warp hits every
+            // bank once per 8 lanes), then whole 512-byte row segments to
+            // every destination -- full lines over NVLink
+            float *st = reinterpret_cast<float *>(smem) + (size_t)quarter * 32 * 132;
+#pragma unroll
+            for (int j = 0; j < BN; j += 4)
+                *reinterpret_cast<float4 *>(st + lane * 132 + j) = make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+            __syncwarp();
+            if (__all_sync(0xffffffffu, ok)) {
+                for (int r = 0; r < 32; r++) {
+                    const float4 v = *reinterpret_cast<const float4 *>(st + r * 132 + lane * 4);
+                    const size_t off = (size_t)(m0 + quarter * 32 + r) * N + n0 + lane * 4;
+                    if (m0 + quarter * 32 + r < M)
+                        for (int d = 0; d < dst->n; d++) *reinterpret_cast<float4 *>(dst->c[d] + off) = v;
+                }
+            }
+        } else if (ok && row < M) {
             float *crow = (splits == 1 ? C : ws + (size_t)split * M * N) + (size_t)row * N + n0;
             if (n0 + BN <= N) {
 #pragma unroll
@@ -498,6 +528,22 @@ extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(BN * NACC))
                      : "memory");
     }
+}
+
+extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
+    sgemm_3xtf32_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_bt,
+                    float *__restrict__ C, int M, int N, int K, float *__restrict__ ws, int splits) {
+    sgemm3x_body<false>(tm_a, tm_bt, C, M, N, K, ws, splits, nullptr);
+}
+
+// The multi-destination form (splits == 1; M, N % 128 == 0): plain stores
+// to local or peer-mapped outputs (never TMA), and a system-scope fence so
+// the peers see them once the kernel completes.
+extern "C" __global__ void __launch_bounds__(t3::THREADS, 1)
+    sgemm_3xtf32_tc_dst(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_bt,
+                        const __grid_constant__ T3Dst dst, int M, int N, int K) {
+    sgemm3x_body<true>(tm_a, tm_bt, nullptr, M, N, K, nullptr, 1, &dst);
+    __threadfence_system();
 }
 
 // out[c][r] = in[r][c] for a rows x cols FP32 matrix (32 x 32 tiles through

@@ -68,6 +68,7 @@ typedef enum {
     F_GEMM_HH_TC,
     F_SPLITK_REDUCE,
     F_SGEMM_3XTF32,
+    F_SGEMM_3XTF32_DST,
     F_TRANSPOSE_F32,
     F_PF_EMBED,
     F_PF_RMS_SPLIT,

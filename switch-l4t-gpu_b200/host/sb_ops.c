@@ -459,6 +459,49 @@ int sb_sgemm_3xtf32(const float *A, const float *B, float *C, int M, int N, int 
     return sgemm3x_launch(c, A, (const float *)(uintptr_t)bt, C, M, N, K, stream);
 }
 
+int sb_sgemm_3xtf32_multi(const float *A, const float *B, float *const *C, int nc, int M, int N, int K,
+                          void *stream) {
+    SB_ARG(A && B && C && nc >= 1 && nc <= SB_SGEMM_MAX_DST, "bad multi-destination sgemm_3xtf32 arguments");
+    SB_ARG(M >= 0 && N >= 0 && K > 0 && M % 128 == 0 && N % 128 == 0 && K % 4 == 0 && ALIGNED16(A) && ALIGNED16(B),
+           "multi-destination sgemm_3xtf32 needs M, N % 128 == 0, K % 4 == 0 and 16-byte aligned operands");
+    /* the kernel's parameter block: T3Dst in csrc/tc_kernels.cu */
+    struct {
+        CUdeviceptr c[SB_SGEMM_MAX_DST];
+        int n;
+    } dst;
+    memset(&dst, 0, sizeof dst);
+    for (int d = 0; d < nc; d++) {
+        SB_ARG(C[d] && ALIGNED16(C[d]), "multi-destination sgemm_3xtf32 needs 16-byte aligned outputs");
+        dst.c[d] = DP(C[d]);
+    }
+    dst.n = nc;
+    sb_ctx *c = sb_ctx_get();
+    if (!c) return SB_ERR_STATE;
+    if (M == 0 || N == 0) return 0;
+    const long tiles = (long)(M / 128) * (N / 128);
+    SB_ARG(tiles < 0x7fffffffL, "multi-destination sgemm_3xtf32: too many tiles");
+    const size_t need = (size_t)K * N * 4; /* Bt = B^T in the library-owned workspace */
+    if (c->tc_bt_bytes < need) {
+        if (c->tc_bt) cuMemFree(c->tc_bt);
+        c->tc_bt = 0;
+        c->tc_bt_bytes = 0;
+        SB_CK(cuMemAlloc(&c->tc_bt, need));
+        c->tc_bt_bytes = need;
+    }
+    CUdeviceptr bsrc = DP(B), bt = c->tc_bt;
+    void *targs[] = {&bsrc, &bt, &K, &N};
+    int rc = sb_launch(c, F_TRANSPOSE_F32, (unsigned)CEIL_DIV(N, 32), (unsigned)CEIL_DIV(K, 32), 32 * 8, 0,
+                       (CUstream)stream, targs, 0);
+    if (rc) return rc;
+    CUtensorMap ta, tb;
+    rc = encode_kmajor_f32(&ta, A, K, M);
+    if (!rc) rc = encode_kmajor_f32(&tb, (const float *)(uintptr_t)bt, K, N);
+    if (rc) return rc;
+    void *args[] = {&ta, &tb, &dst, &M, &N, &K};
+    const unsigned smem = 1024 + 3 * 65536 + 256;
+    return sb_launch(c, F_SGEMM_3XTF32_DST, (unsigned)tiles, 1, 192, smem, (CUstream)stream, args, 0);
+}
+
 int sb_sgemm_nt_3xtf32(const float *A, const float *Bt, float *C, int M, int N, int K, void *stream) {
     SB_ARG(A && Bt && C && M >= 0 && N >= 0 && K > 0, "bad sgemm_nt_3xtf32 arguments");
     SB_ARG(K % 4 == 0 && N % 4 == 0 && ALIGNED16(A) && ALIGNED16(Bt) && ALIGNED16(C),

@@ -87,6 +87,7 @@ static const struct {
     [F_SPLITK_REDUCE] = {M_TC, "gemm_splitk_reduce"},
     [F_SPLITK_REDUCE4] = {M_TC, "gemm_splitk_reduce4"},
     [F_SGEMM_3XTF32] = {M_TC, "sgemm_3xtf32_tc"},
+    [F_SGEMM_3XTF32_DST] = {M_TC, "sgemm_3xtf32_tc_dst"},
     [F_TRANSPOSE_F32] = {M_TC, "transpose_f32"},
     [F_PF_EMBED] = {M_QWEN, "qwen_pf_embed"},
     [F_PF_RMS_SPLIT] = {M_QWEN, "qwen_pf_rms_split"},

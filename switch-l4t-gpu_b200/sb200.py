@@ -90,6 +90,7 @@ def lib():
     _sig(L.sb_gemm_hh, I, P, P, P, I, I, I, P)
     _sig(L.sb_tc_error, I, P)
     _sig(L.sb_sgemm_3xtf32, I, P, P, P, I, I, I, P)
+    _sig(L.sb_sgemm_3xtf32_multi, I, P, P, ctypes.POINTER(P), I, I, I, I, P)
     _sig(L.sb_rmsnorm, I, P, P, P, I, F, I, P)
     _sig(L.sb_rope, I, P, P, P, I, I, I, I, P)
     _sig(L.sb_swiglu, I, P, P, P, I, P)
@@ -263,6 +264,12 @@ def sample_topk(idx, val, top_p, state):
     idx = np.ascontiguousarray(idx, dtype=np.int32)
     val = np.ascontiguousarray(val, dtype=np.float32)
     return lib().sb_sample_topk(idx.ctypes.data, val.ctypes.data, len(idx), top_p, ctypes.byref(state))
+
+
+def sgemm_3xtf32_multi(A, B, outs, M, N, K, stream=None):
+    """The 3xTF32 SGEMM stored into every matrix of `outs`: sb_sgemm_3xtf32_multi."""
+    arr = (ctypes.c_void_p * len(outs))(*[_p(c) for c in outs])
+    check(lib().sb_sgemm_3xtf32_multi(_p(A), _p(B), arr, len(outs), M, N, K, _s(stream)))
 
 
 def sgemm_3xtf32(A, B, C, M, N, K, stream=None):

@@ -67,7 +67,7 @@ class PanelSgemm:
     kernel:  "fp32" (CUDA-core FFMA, the default) or "3xtf32" (opt-in, the
              TF32 tensor pipe with the 3xTF32 split).
     gather_mode: "nccl" (the panel, then an NCCL all-gather) or "peer" (the
-             fp32 kernel stores every tile into every rank's C; needs M a
+             kernel stores every tile into every rank's C; needs M a
              multiple of 128 x world, N of 128 and K of 16; call close()
              on every rank before the buffers go away).
     """
@@ -101,8 +101,9 @@ class PanelSgemm:
         self.gather_mode = gather_mode if self.world > 1 else "nccl"
         self._peers = {}
         if self.gather_mode == "peer":
-            if kernel != "fp32" or compute is not None or self.chunks != 1 or not self.is_cuda:
-                raise ValueError("PanelSgemm: peer gather runs the fp32 CUDA kernel, chunks=1")
+            if compute is not None or self.chunks != 1 or not self.is_cuda:
+                raise ValueError("PanelSgemm: peer gather runs this package's CUDA kernels, chunks=1")
+            self._multi = "sgemm_multi" if kernel == "fp32" else "sgemm_3xtf32_multi"
             if M % (128 * self.world) or N % 128 or K % 16:
                 raise ValueError("PanelSgemm: peer gather needs M % (128 x world) == 0, N % 128 == 0, K % 16 == 0")
             self._open_peers()
@@ -174,7 +175,7 @@ class PanelSgemm:
             s = self._stream(stream)
             with torch.cuda.stream(s):
                 dist.all_reduce(self._flag, op=dist.ReduceOp.MAX, group=self.group)  # the previous C is read
-                sb200.sgemm_multi(A_panel, B, self._dsts, self.rows, self.N, self.K, s)
+                getattr(sb200, self._multi)(A_panel, B, self._dsts, self.rows, self.N, self.K, s)
                 dist.all_reduce(self._flag, op=dist.ReduceOp.MAX, group=self.group)  # every panel has landed
             return self.C
         if self.chunks == 1:

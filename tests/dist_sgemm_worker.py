@@ -23,7 +23,7 @@ import sgemm_dist  # noqa: E402
 
 
 CASES = [(1000, 384, 1002, 1, "nccl"), (2048, 512, 256, 3, "nccl"), (257, 129, 67, 2, "nccl"),
-         (1024, 512, 256, 1, "peer"), (2048, 1024, 512, 1, "peer")]
+         (1024, 512, 256, 1, "peer"), (2048, 1024, 512, 1, "peer"), (2048, 1024, 512, 1, "peer3x")]
 
 
 def main():
@@ -37,10 +37,12 @@ def main():
         for ci, (M, N, K, chunks, mode) in enumerate(CASES):
             A = sb200.synth_uniform(M * K, -1.0, 1.0, 10 + ci).reshape(M, K)
             B = sb200.synth_uniform(K * N, -1.0, 1.0, 20 + ci).reshape(K, N)
-            ps = sgemm_dist.PanelSgemm(M, N, K, chunks=chunks, gather_mode=mode)
+            kern = "3xtf32" if mode == "peer3x" else "fp32"
+            ps = sgemm_dist.PanelSgemm(M, N, K, chunks=chunks, gather_mode="nccl" if mode == "nccl" else "peer",
+                                       kernel=kern)
             Ap = torch.from_numpy(A[ps.row0:ps.row1].copy()).to(dev)
             Bd = torch.from_numpy(B).to(dev)
-            if mode == "peer":
+            if mode != "nccl":
                 ps.C.fill_(float("nan"))  # every cell must be written, by some rank
                 torch.cuda.synchronize()
                 dist.barrier()

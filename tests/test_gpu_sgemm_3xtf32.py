@@ -86,3 +86,30 @@ def test_3xtf32_16384_accuracy(cuda_dev):
     assert sb200.tc_error() == 0
     rel = orc.freivalds(A.cpu().numpy(), B.cpu().numpy(), C.cpu().numpy())
     assert rel <= REL_FROB, f"freivalds {rel:.2e}"
+
+
+@pytest.mark.parametrize("M,N,K,nout", [(2048, 2048, 512, 2), (256, 384, 64, 3)])
+def test_3xtf32_multi_outputs(cuda_dev, M, N, K, nout):
+    """sb_sgemm_3xtf32_multi stores every row of every tile into each output
+    (here all on this GPU): every output within the FP32 bar of the harness
+    loop, all outputs identical, and bit-identical to sb_sgemm_3xtf32 when
+    that call needs no K split (tiles >= SMs)."""
+    import torch
+    A = sb200.synth_uniform(M * K, -1.0, 1.0, 61).reshape(M, K)
+    B = sb200.synth_uniform(K * N, -1.0, 1.0, 62).reshape(K, N)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    outs = [torch.full((M, N), float("nan"), device="cuda") for _ in range(nout)]
+    sb200.sgemm_3xtf32_multi(dA, dB, outs, M, N, K)
+    torch.cuda.synchronize()
+    assert sb200.tc_error() == 0
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    if (M // 128) * (N // 128) >= sb200.sm_count():
+        one = torch.zeros((M, N), device="cuda")
+        sb200.sgemm_3xtf32(dA, dB, one, M, N, K)
+        torch.cuda.synchronize()
+        assert torch.equal(outs[0], one)
+    C = outs[0].cpu().numpy()
+    rows = sorted({0, M // 2, M - 1})
+    ref = np.stack([orc.sgemm(A, B, r, r + 1)[r] for r in rows])
+    assert np.linalg.norm(C[rows] - ref) <= 1e-5 * np.linalg.norm(ref)
