@@ -134,3 +134,32 @@ def test_rank_leaving_between_steps_fails_fast(tmp_path):
     outcome, secs = (tmp_path / "leaver.txt").read_text().splitlines()[:2]
     assert outcome.startswith("error"), outcome
     assert float(secs) < 30.0
+
+
+def test_rejects_bad_gather_mode():
+    with pytest.raises(ValueError):
+        sgemm_dist.PanelSgemm(4, 4, 4, device="cpu", compute=_exact_compute, gather_mode="bogus")
+
+
+def _peer_on_cpu_main(rank, world, port, outdir):
+    """The peer gather stores from this package's CUDA kernels into the
+    other ranks' C; on CPU ranks (gloo) it must refuse at construction,
+    before any collective, on every rank alike."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    outcome = "accepted"
+    try:
+        sgemm_dist.PanelSgemm(256, 128, 16, device="cpu", gather_mode="peer")
+    except ValueError as ex:
+        outcome = "ValueError: " + str(ex)
+    with open(os.path.join(outdir, f"peer_cpu_{rank}.txt"), "w") as f:
+        f.write(outcome + "\n")
+    dist.destroy_process_group()
+
+
+def test_peer_gather_refused_on_cpu_ranks(tmp_path):
+    mp.start_processes(_peer_on_cpu_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    for r in range(2):
+        text = (tmp_path / f"peer_cpu_{r}.txt").read_text()
+        assert text.startswith("ValueError") and "CUDA" in text, text
